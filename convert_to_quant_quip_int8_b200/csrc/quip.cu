@@ -1,0 +1,341 @@
+// K4: offline QuIP Hadamard conversion of one weight matrix on the GPU.
+//
+// Reference (converters/quip_int8.py, identity Hessian):
+//   W' = FHT_N(FHT_M(pad(W) * s_u * s_v^T))                        :539-551
+//   s' = clamp(rowamax(W') / 127, 1e-12); Q' = clamp(round(W'/s'), +-127)  :1272-1274, 655
+//   W_d = slice(FHT_M(FHT_N(Q' * s')) * s_u * s_v)                   :1452, 1489-1506
+//   requant of W_d with per-row / global / per-(row, K-block) scales :1614-1669
+// FHT_* is the normalized 1-D transform along one dimension; the M-direction
+// (down the columns) runs first on the way in and last on the way out, as
+// in the reference, because fp32 rounding depends on that order.
+//
+// GPU plan (fp32 workspace X = [M_pad, N_pad]):
+//   col_fwht (1-2 passes): bf16/f32 W -> signs -> M-direction stages -> X
+//   quip_row:  one CTA per row: FHT_N, RTN to int8, dequant, FHT_N -> X
+//   col_fwht (1-2 passes): M-direction stages -> signs -> slice -> W_d
+//   requant_{row,block,global}: W_d -> int8 + scales
+// A column pass holds up to 512 rows x 32 columns in shared memory and
+// performs the butterfly stages of a contiguous range of row-index bits;
+// ranges run in ascending order, so the stage order equals the reference's.
+#include <cmath>
+#include <cstdint>
+
+#include "common.cuh"
+#include "fwht_row.cuh"
+
+namespace qi8 {
+namespace {
+
+constexpr int COL_STRIP = 32;
+constexpr int COL_THREADS = 256;
+constexpr int COL_MAX_BITS = 9;
+
+struct ColArgs {
+  const void* w;  // first forward pass: source weight [M, N]
+  int w_dtype;
+  int64_t M, N, M_pad, N_pad;
+  float* x;  // workspace [M_pad, N_pad]
+  const float* s_u;
+  const float* s_v;
+  int b0, rbits;  // this pass transforms row-index bits [b0, b0 + rbits)
+  float norm;
+  float* dst;  // inverse last pass: W_d destination [M, N] with row stride ld_dst
+  int64_t ld_dst;
+};
+
+template <bool LOAD_W, bool NORM, bool SIGN_OUT>
+__global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
+  extern __shared__ float tile[];  // [R][COL_STRIP]
+  const int R = 1 << a.rbits;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NW = COL_THREADS / 32;
+  const int64_t j = (int64_t)blockIdx.x * COL_STRIP + lane;
+  const bool col_ok = j < a.N_pad;
+  const int64_t lo_count = int64_t(1) << a.b0;
+  const int64_t lo = blockIdx.y % lo_count, hi = blockIdx.y / lo_count;
+  const int64_t hi_base = lo + (hi << (a.b0 + a.rbits));
+
+  for (int k = warp; k < R; k += NW) {
+    const int64_t i = hi_base + ((int64_t)k << a.b0);
+    float v = 0.0f;
+    if (col_ok) {
+      if constexpr (LOAD_W) {
+        v = (i < a.M && j < a.N) ? load_as_f32(a.w, a.w_dtype, i * a.N + j) : 0.0f;
+        v = __fmul_rn(v, __ldg(a.s_u + i));
+        v = __fmul_rn(v, __ldg(a.s_v + j));
+      } else {
+        v = a.x[i * a.N_pad + j];
+      }
+    }
+    tile[k * COL_STRIP + lane] = v;
+  }
+  __syncthreads();
+  for (int h = 1; h < R; h <<= 1) {
+    for (int p = warp; p < (R >> 1); p += NW) {
+      const int k = ((p / h) * 2 * h) + (p % h);
+      const float lo_v = tile[k * COL_STRIP + lane];
+      const float hi_v = tile[(k + h) * COL_STRIP + lane];
+      tile[k * COL_STRIP + lane] = lo_v + hi_v;
+      tile[(k + h) * COL_STRIP + lane] = lo_v - hi_v;
+    }
+    __syncthreads();
+  }
+  for (int k = warp; k < R; k += NW) {
+    const int64_t i = hi_base + ((int64_t)k << a.b0);
+    float v = tile[k * COL_STRIP + lane];
+    if constexpr (NORM) v = __fmul_rn(v, a.norm);
+    if constexpr (SIGN_OUT) {
+      if (i < a.M && j < a.N) {
+        v = __fmul_rn(v, __ldg(a.s_u + i));
+        v = __fmul_rn(v, __ldg(a.s_v + j));
+        a.dst[i * a.ld_dst + j] = v;
+      }
+    } else {
+      if (col_ok) a.x[i * a.N_pad + j] = v;
+    }
+  }
+}
+
+struct RowArgs {
+  float* x;
+  int64_t ld_x;
+  float norm;
+  int8_t* q_rot;  // optional [M_pad, N_pad]
+  float* s_rot;   // optional [M_pad]
+};
+
+template <int L>
+__global__ void __launch_bounds__(RotCfg<L>::THREADS) quip_row_kernel(RowArgs a) {
+  using C = RotCfg<L>;
+  constexpr int E = C::E, P = C::P;
+  extern __shared__ float4 dyn_smem[];
+  float* buf = reinterpret_cast<float*>(dyn_smem);
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  const bool active = t < P;
+  const int64_t row = blockIdx.x;
+  float* xr = a.x + row * a.ld_x;
+  const int c0 = t * E;
+  float v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = active ? xr[c0 + e] : 0.0f;
+
+  fwht_row<L>(v, buf);
+  float local = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    v[e] = __fmul_rn(v[e], a.norm);
+    local = fmaxf(local, fabsf(v[e]));
+  }
+  const float amax = block_max(local, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  int8_t q[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) q[e] = rint_clamp(__fdiv_rn(v[e], s), -127.0f, 127.0f);
+  if (a.q_rot && active) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) a.q_rot[row * C::N + c0 + e] = q[e];
+  }
+  if (a.s_rot && t == 0) a.s_rot[row] = s;
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = __fmul_rn((float)q[e], s);
+  fwht_row<L>(v, buf);
+  if (active) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) xr[c0 + e] = __fmul_rn(v[e], a.norm);
+  }
+}
+
+template <int L>
+int launch_row_L(const RowArgs& a, int64_t rows, cudaStream_t st) {
+  using C = RotCfg<L>;
+  auto kern = quip_row_kernel<L>;
+  if (C::SMEM > 48 * 1024)
+    QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+  kern<<<(unsigned)rows, C::THREADS, C::SMEM, st>>>(a);
+  return check_cuda(cudaGetLastError(), "quip_row_kernel launch");
+}
+
+int launch_row(int L, const RowArgs& a, int64_t rows, cudaStream_t st) {
+  switch (L) {
+#define QI8_CASE(l) case l: return launch_row_L<l>(a, rows, st);
+    QI8_CASE(0) QI8_CASE(1) QI8_CASE(2) QI8_CASE(3) QI8_CASE(4) QI8_CASE(5) QI8_CASE(6) QI8_CASE(7)
+    QI8_CASE(8) QI8_CASE(9) QI8_CASE(10) QI8_CASE(11) QI8_CASE(12) QI8_CASE(13) QI8_CASE(14)
+    QI8_CASE(15)
+#undef QI8_CASE
+    default: return fail(QI8_ESHAPE, "row length 2^%d out of range", L);
+  }
+}
+
+// ------------------------------------------------------------- requant
+struct ReqArgs {
+  const float* w;
+  int64_t ld_w, M, N;
+  int8_t* q;
+  float* scale;
+  int block;
+  const unsigned int* gmax;
+};
+
+__global__ void __launch_bounds__(256) requant_row_kernel(ReqArgs a) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float* wr = a.w + row * a.ld_w;
+  float local = 0.0f;
+  for (int64_t c = threadIdx.x; c < a.N; c += blockDim.x) local = fmaxf(local, fabsf(wr[c]));
+  const float amax = block_max(local, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  for (int64_t c = threadIdx.x; c < a.N; c += blockDim.x)
+    a.q[row * a.N + c] = rint_clamp(__fdiv_rn(wr[c], s), -127.0f, 127.0f);
+  if (threadIdx.x == 0) a.scale[row] = s;
+}
+
+__global__ void __launch_bounds__(256) requant_block_kernel(ReqArgs a) {
+  const int64_t row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per = a.block / 32;  // 1, 2 or 4
+  const int64_t nb = a.N / a.block;
+  const float* wr = a.w + row * a.ld_w;
+  for (int64_t b = warp; b < nb; b += 8) {
+    float v[4];
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = k < per ? wr[b * a.block + k * 32 + lane] : 0.0f;
+      m = fmaxf(m, fabsf(v[k]));
+    }
+    m = warp_max(m);
+    const float s = fmaxf(__fdiv_rn(m, 127.0f), 1e-12f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (k < per) a.q[row * a.N + b * a.block + k * 32 + lane] = rint_clamp(__fdiv_rn(v[k], s), -127.0f, 127.0f);
+    if (lane == 0) a.scale[row * nb + b] = s;
+  }
+}
+
+__global__ void absmax_rows_kernel(const float* __restrict__ w, int64_t ld_w, int64_t M, int64_t N,
+                                   unsigned int* __restrict__ out) {
+  float m = 0.0f;
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / N, c = i - r * N;
+    m = fmaxf(m, fabsf(w[r * ld_w + c]));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+__global__ void requant_global_kernel(ReqArgs a) {
+  const float s = fmaxf(__fdiv_rn(__uint_as_float(*a.gmax), 127.0f), 1e-12f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) a.scale[0] = s;
+  const int64_t total = a.M * a.N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / a.N, c = i - r * a.N;
+    a.q[i] = rint_clamp(__fdiv_rn(a.w[r * a.ld_w + c], s), -127.0f, 127.0f);
+  }
+}
+
+int64_t next_pow2(int64_t n) {
+  int64_t p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// Runs the M-direction transform over X in passes of <= COL_MAX_BITS bits.
+int col_passes(bool forward, const ColArgs& base, cudaStream_t st) {
+  const int L = log2_exact(base.M_pad);
+  int b0 = 0;
+  while (b0 < L || (L == 0 && b0 == 0)) {
+    const int rb = (L - b0) > COL_MAX_BITS ? COL_MAX_BITS : (L - b0);
+    ColArgs a = base;
+    a.b0 = b0;
+    a.rbits = rb;
+    const bool first = (b0 == 0), last = (b0 + rb == L);
+    const size_t smem = sizeof(float) * COL_STRIP * ((size_t)1 << rb);
+    dim3 grid((unsigned)((base.N_pad + COL_STRIP - 1) / COL_STRIP), (unsigned)(base.M_pad >> rb));
+    void (*kern)(ColArgs) = nullptr;
+    if (forward) {
+      if (first && last) kern = col_fwht_kernel<true, true, false>;
+      else if (first) kern = col_fwht_kernel<true, false, false>;
+      else if (last) kern = col_fwht_kernel<false, true, false>;
+      else kern = col_fwht_kernel<false, false, false>;
+    } else {
+      kern = last ? col_fwht_kernel<false, true, true> : col_fwht_kernel<false, false, false>;
+    }
+    if (smem > 48 * 1024) QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, COL_THREADS, smem, st>>>(a);
+    QI8_CUDA(cudaGetLastError());
+    if (L == 0) break;
+    b0 += rb;
+  }
+  return QI8_OK;
+}
+
+}  // namespace
+}  // namespace qi8
+
+using namespace qi8;
+
+extern "C" {
+
+int64_t qi8_quip_workspace_bytes(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  return next_pow2(M) * next_pow2(N) * 4 + 256;
+}
+
+int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, const float* s_u, const float* s_v,
+                     int store_transformed, int requant, int block, int8_t* q_out, float* scale_out,
+                     float* dequant_out, void* workspace, int64_t workspace_bytes, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(w && s_u && s_v && q_out && scale_out && workspace, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(M > 0 && N > 0, QI8_ESHAPE, "bad sizes M=%lld N=%lld", (long long)M, (long long)N);
+  QI8_REQUIRE(w_dtype == QI8_BF16 || w_dtype == QI8_F16 || w_dtype == QI8_F32, QI8_EDTYPE, "weight dtype %d", w_dtype);
+  const int64_t M_pad = next_pow2(M), N_pad = next_pow2(N);
+  QI8_REQUIRE(M_pad <= 32768 && N_pad <= 32768, QI8_ESHAPE, "padded size %lldx%lld exceeds 32768",
+              (long long)M_pad, (long long)N_pad);
+  QI8_REQUIRE(workspace_bytes >= qi8_quip_workspace_bytes(M, N), QI8_EINVAL, "workspace too small (%lld < %lld)",
+              (long long)workspace_bytes, (long long)qi8_quip_workspace_bytes(M, N));
+  QI8_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, QI8_EALIGN, "workspace must be 256-byte aligned");
+  QI8_REQUIRE(requant == QI8_REQ_ROW || requant == QI8_REQ_GLOBAL || requant == QI8_REQ_BLOCK, QI8_EINVAL,
+              "requant scheme %d", requant);
+  if (requant == QI8_REQ_BLOCK && !store_transformed)
+    QI8_REQUIRE(block == 32 || block == 64 || block == 128, QI8_ESHAPE, "block size %d not in {32, 64, 128}", block);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  float* X = static_cast<float*>(workspace);
+  unsigned int* gword = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + M_pad * N_pad * 4);
+
+  ColArgs ca{};
+  ca.w = w; ca.w_dtype = w_dtype; ca.M = M; ca.N = N; ca.M_pad = M_pad; ca.N_pad = N_pad; ca.x = X;
+  ca.s_u = s_u; ca.s_v = s_v;
+  ca.norm = (float)(1.0 / std::sqrt((double)M_pad));
+  float* wd = dequant_out ? dequant_out : X;
+  const int64_t ld_wd = dequant_out ? N : N_pad;
+  ca.dst = wd; ca.ld_dst = ld_wd;
+
+  int rc = col_passes(true, ca, st);
+  if (rc) return rc;
+  RowArgs ra{X, N_pad, (float)(1.0 / std::sqrt((double)N_pad)), store_transformed ? q_out : nullptr,
+             store_transformed ? scale_out : nullptr};
+  rc = launch_row(log2_exact(N_pad), ra, M_pad, st);
+  if (rc) return rc;
+  rc = col_passes(false, ca, st);
+  if (rc) return rc;
+  if (store_transformed) return QI8_OK;
+
+  ReqArgs qa{wd, ld_wd, M, N, q_out, scale_out, block, gword};
+  if (requant == QI8_REQ_BLOCK && N % block != 0) requant = QI8_REQ_ROW;
+  if (requant == QI8_REQ_ROW) {
+    requant_row_kernel<<<(unsigned)M, 256, 0, st>>>(qa);
+  } else if (requant == QI8_REQ_BLOCK) {
+    requant_block_kernel<<<(unsigned)M, 256, 0, st>>>(qa);
+  } else {
+    QI8_CUDA(cudaMemsetAsync(gword, 0, 4, st));
+    const int sms = sm_count() > 0 ? sm_count() : 148;
+    absmax_rows_kernel<<<sms * 4, 256, 0, st>>>(wd, ld_wd, M, N, gword);
+    requant_global_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  }
+  return check_cuda(cudaGetLastError(), "requant launch");
+}
+
+}  // extern "C"

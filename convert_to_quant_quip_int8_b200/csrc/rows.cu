@@ -1,0 +1,592 @@
+// Row kernels of the QuIP W8A8 path (HBM-bound):
+//   * qi8_quant_rows       -- per-token / per-128-block int8 quantization
+//   * qi8_rotate_quant_rows (K1) -- sign + FWHT + quantization, one pass
+//   * qi8_fwht_rows        -- sign + FWHT (+ sign) to fp32
+//   * qi8_unrotate_rows    (K3) -- FWHT + sign + slice + bias -> bf16/f16/f32
+//   * qi8_dequant, qi8_quant_weight -- layout (de)quantizers
+//
+// One CTA per row.  The FWHT core (fwht_row.cuh) reproduces the reference's
+// butterfly order bit for bit; the normalization is one fp32 multiply by
+// float(1/sqrt(n)) (utils/hadamard.py:155-157).  Quantization follows the
+// reference rule selected by the mode (see qi8.h).
+#include <cstdint>
+#include <cmath>
+
+#include "common.cuh"
+#include "fwht_row.cuh"
+
+namespace qi8 {
+namespace {
+
+// ------------------------------------------------------------------ loads
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+// Loads E consecutive elements starting at column c0 of a row (zero beyond n).
+template <typename T, int E>
+__device__ __forceinline__ void load_run(const T* __restrict__ row, int c0, int n, bool vec, float (&v)[E]) {
+  constexpr int BYTES = E * (int)sizeof(T);
+  if constexpr (BYTES >= 16 && BYTES % 16 == 0) {
+    if (vec && c0 + E <= n) {
+      const uint4* p = reinterpret_cast<const uint4*>(row + c0);
+#pragma unroll
+      for (int k = 0; k < BYTES / 16; ++k) {
+        uint4 u = __ldg(p + k);
+        const T* tv = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int j = 0; j < 16 / (int)sizeof(T); ++j) v[k * (16 / sizeof(T)) + j] = to_f32<T>(tv[j]);
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    int c = c0 + e;
+    v[e] = c < n ? to_f32<T>(row[c]) : 0.0f;
+  }
+}
+
+// Stores E int8 values to dst (dst aligned to E bytes when E is 4/8/16/32).
+template <int E>
+__device__ __forceinline__ void store_i8_run(int8_t* dst, const int8_t (&q)[E]) {
+  if constexpr (E % 16 == 0) {
+#pragma unroll
+    for (int k = 0; k < E / 16; ++k) reinterpret_cast<uint4*>(dst)[k] = reinterpret_cast<const uint4*>(q)[k];
+  } else if constexpr (E == 8) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(q);
+  } else if constexpr (E == 4) {
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(q);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) dst[e] = q[e];
+  }
+}
+
+// ================================================== non-rotated row quant
+struct QArgs {
+  const void* x;
+  int64_t ld_x;
+  int n;
+  int8_t* q;
+  int64_t ld_q;
+  float* scale;
+  int vec;  // x rows 16B aligned and q rows 8B aligned
+};
+
+constexpr int QR_THREADS = 256;
+
+template <typename T, int CPT, int MODE>
+__global__ void __launch_bounds__(QR_THREADS) quant_rows_kernel(QArgs a) {
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
+  int8_t* qr = a.q + row * a.ld_q;
+  const int nc = a.n >> 3;  // chunks of 8
+  float v[CPT][8];
+  float local = 0.0f;
+#pragma unroll
+  for (int r = 0; r < CPT; ++r) {
+    int c = r * QR_THREADS + t;
+    if (c < nc) {
+      load_run<T, 8>(xr, c * 8, a.n, a.vec != 0, v[r]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[r][e] = 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) local = fmaxf(local, fabsf(v[r][e]));
+  }
+  if constexpr (MODE == QI8_Q_TOKEN) {
+    const float amax = block_max(local, red);
+    const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float rcp = __frcp_rn(s);
+#pragma unroll
+    for (int r = 0; r < CPT; ++r) {
+      int c = r * QR_THREADS + t;
+      if (c < nc) {
+        int8_t q8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q8[e] = rint_clamp(__fmul_rn(v[r][e], rcp), -128.0f, 127.0f);
+        if (a.vec) store_i8_run<8>(qr + c * 8, q8);
+        else
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qr[c * 8 + e] = q8[e];
+      }
+    }
+    if (t == 0) a.scale[row] = s;
+  } else {
+    // 128-element blocks = 16 consecutive chunks = 16 consecutive lanes
+    const int nb = a.n >> 7;
+#pragma unroll
+    for (int r = 0; r < CPT; ++r) {
+      int c = r * QR_THREADS + t;
+      float m = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[r][e]));
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float s = __fdiv_rn(m, 127.0f);
+      if (c < nc) {
+        int8_t q8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q8[e] = trunc_sat(__fdiv_rn(v[r][e], s));
+        if (a.vec) store_i8_run<8>(qr + c * 8, q8);
+        else
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qr[c * 8 + e] = q8[e];
+        if ((t & 15) == 0) a.scale[row * nb + (c >> 4)] = s;
+      }
+    }
+  }
+}
+
+// Scalar fallback for rows whose width is not a multiple of 8 (TOKEN) or
+// whose pointers are not vector aligned; reads the row twice.
+template <typename T>
+__global__ void __launch_bounds__(QR_THREADS) quant_rows_scalar_kernel(QArgs a) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
+  int8_t* qr = a.q + row * a.ld_q;
+  float local = 0.0f;
+  for (int c = threadIdx.x; c < a.n; c += blockDim.x) local = fmaxf(local, fabsf(to_f32<T>(xr[c])));
+  const float amax = block_max(local, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+  const float rcp = __frcp_rn(s);
+  for (int c = threadIdx.x; c < a.n; c += blockDim.x)
+    qr[c] = rint_clamp(__fmul_rn(to_f32<T>(xr[c]), rcp), -128.0f, 127.0f);
+  if (threadIdx.x == 0) a.scale[row] = s;
+}
+
+// ================================================ rotated rows (FWHT) core
+enum RotOut { RO_Q_TOKEN = 0, RO_Q_BLOCK = 1, RO_F32 = 2, RO_UNROT = 3 };
+
+struct RotArgs {
+  const void* x;
+  int64_t ld_x;
+  int n_in;
+  const float* pre_sign;
+  const float* post_sign;
+  float norm;
+  int do_norm;
+  int vec;
+  // RO_Q_*: q [rows, N] (16B-aligned rows), scale [rows] or [rows, N/128]
+  int8_t* q;
+  float* scale;
+  // RO_F32: f_out [rows, N]
+  float* f_out;
+  // RO_UNROT
+  const void* bias;
+  int bias_dtype;
+  int n_out;
+  void* out;
+  int out_dtype;
+  int64_t ld_out;
+};
+
+template <int L, typename T, int OUT>
+__global__ void __launch_bounds__(RotCfg<L>::THREADS) rotate_rows_kernel(RotArgs a) {
+  using C = RotCfg<L>;
+  constexpr int N = C::N, E = C::E, P = C::P;
+  extern __shared__ float4 dyn_smem[];
+  float* buf = reinterpret_cast<float*>(dyn_smem);
+  __shared__ float red[32];
+
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const bool active = t < P;
+  const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
+
+  float v[E];
+  const int c0 = t * E;
+  if (active) {
+    load_run<T, E>(xr, c0, a.n_in, a.vec != 0, v);
+    if (a.pre_sign) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = __fmul_rn(v[e], __ldg(a.pre_sign + c0 + e));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = 0.0f;
+  }
+
+  fwht_row<L>(v, buf);
+
+  if (a.do_norm) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = __fmul_rn(v[e], a.norm);
+  }
+
+  if constexpr (OUT == RO_Q_TOKEN) {
+    float local = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) local = fmaxf(local, fabsf(v[e]));
+    const float amax = block_max(local, red);
+    const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float rcp = __frcp_rn(s);
+    if (active) {
+      int8_t q8[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) q8[e] = rint_clamp(__fmul_rn(v[e], rcp), -128.0f, 127.0f);
+      store_i8_run<E>(a.q + row * N + c0, q8);
+    }
+    if (t == 0) a.scale[row] = s;
+  } else if constexpr (OUT == RO_Q_BLOCK) {
+    static_assert(E >= 4 || N < 128, "block mode needs >= 4 elements per thread");
+    constexpr int G = (128 / E) < 32 ? (128 / E) : 32;  // lanes per 128-block
+    float m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) m = fmaxf(m, fabsf(v[e]));
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float s = __fdiv_rn(m, 127.0f);
+    if (active) {
+      int8_t q8[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) q8[e] = trunc_sat(__fdiv_rn(v[e], s));
+      store_i8_run<E>(a.q + row * N + c0, q8);
+      if ((t % G) == 0) a.scale[row * (N / 128) + c0 / 128] = s;
+    }
+  } else if constexpr (OUT == RO_F32) {
+    if (active) {
+      if (a.post_sign) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = __fmul_rn(v[e], __ldg(a.post_sign + c0 + e));
+      }
+      float* dst = a.f_out + row * N + c0;
+      if constexpr (E % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < E / 4; ++k)
+          reinterpret_cast<float4*>(dst)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) dst[e] = v[e];
+      }
+    }
+  } else {  // RO_UNROT
+    if (active) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int c = c0 + e;
+        if (c < a.n_out) {
+          float y = v[e];
+          if (a.post_sign) y = __fmul_rn(y, __ldg(a.post_sign + c));
+          if (a.bias) y = __fadd_rn(y, load_as_f32(a.bias, a.bias_dtype, c));
+          store_from_f32(a.out, a.out_dtype, row * a.ld_out + c, y);
+        }
+      }
+    }
+  }
+}
+
+template <int L, typename T, int OUT>
+int launch_rotate_L(const RotArgs& a, int64_t rows, cudaStream_t st) {
+  using C = RotCfg<L>;
+  auto kern = rotate_rows_kernel<L, T, OUT>;
+  if (C::SMEM > 48 * 1024) {
+    QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+  }
+  kern<<<(unsigned)rows, C::THREADS, C::SMEM, st>>>(a);
+  return check_cuda(cudaGetLastError(), "rotate_rows_kernel launch");
+}
+
+template <typename T, int OUT>
+int launch_rotate(int L, const RotArgs& a, int64_t rows, cudaStream_t st) {
+  switch (L) {
+#define QI8_CASE(l) case l: return launch_rotate_L<l, T, OUT>(a, rows, st);
+    QI8_CASE(1) QI8_CASE(2) QI8_CASE(3) QI8_CASE(4) QI8_CASE(5) QI8_CASE(6) QI8_CASE(7)
+    QI8_CASE(8) QI8_CASE(9) QI8_CASE(10) QI8_CASE(11) QI8_CASE(12) QI8_CASE(13) QI8_CASE(14)
+    QI8_CASE(15)
+#undef QI8_CASE
+    default: return fail(QI8_ESHAPE, "n_pad = 2^%d out of range [2, 32768]", L);
+  }
+}
+
+template <int OUT>
+int launch_rotate_dtype(int x_dtype, int L, const RotArgs& a, int64_t rows, cudaStream_t st) {
+  switch (x_dtype) {
+    case QI8_BF16: return launch_rotate<__nv_bfloat16, OUT>(L, a, rows, st);
+    case QI8_F16: return launch_rotate<__half, OUT>(L, a, rows, st);
+    case QI8_F32: return launch_rotate<float, OUT>(L, a, rows, st);
+    default: return fail(QI8_EDTYPE, "input dtype %d not in {bf16, f16, f32}", x_dtype);
+  }
+}
+
+// ================================================================ dequant
+__global__ void dequant_kernel(const int8_t* __restrict__ q, int64_t rows, int64_t n,
+                               const float* __restrict__ scale, int kind, int block, void* out,
+                               int out_dtype) {
+  const int64_t total = rows * n;
+  const int64_t nb = block > 0 ? (n + block - 1) / block : 1;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n, c = i - r * n;
+    float s;
+    switch (kind) {
+      case QI8_S_SCALAR: s = scale[0]; break;
+      case QI8_S_ROW: s = scale[r]; break;
+      case QI8_S_ROW_KBLOCK: s = scale[r * nb + c / block]; break;
+      default: s = scale[(r / block) * nb + c / block]; break;  // TILE128
+    }
+    store_from_f32(out, out_dtype, i, __fmul_rn((float)q[i], s));
+  }
+}
+
+// ====================================================== weight quantizers
+template <typename T>
+__global__ void absmax_kernel(const T* __restrict__ w, int64_t total, unsigned int* __restrict__ out) {
+  float m = 0.0f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(to_f32<T>(w[i])));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));  // m >= 0: uint order == float order
+}
+
+template <typename T>
+__global__ void quant_tensorwise_kernel(const T* __restrict__ w, int64_t total,
+                                        const unsigned int* __restrict__ amax_bits,
+                                        int8_t* __restrict__ q, float* __restrict__ scale_out) {
+  const float amax = __uint_as_float(*amax_bits);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+  const float rcp = __frcp_rn(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = s;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x)
+    q[i] = rint_clamp(__fmul_rn(to_f32<T>(w[i]), rcp), -128.0f, 127.0f);
+}
+
+// Triton weight_quant semantics: one CTA per 128x128 tile.
+template <typename T>
+__global__ void __launch_bounds__(256) quant_tile128_kernel(const T* __restrict__ w, int64_t rows, int64_t n,
+                                                           int8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ float red[32];
+  const int64_t tr = blockIdx.y, tc = blockIdx.x;
+  const int64_t nbc = (n + 127) / 128;
+  float v[64];
+  float local = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 64; ++k) {
+    const int idx = k * 256 + threadIdx.x;
+    const int64_t r = tr * 128 + idx / 128, c = tc * 128 + idx % 128;
+    v[k] = (r < rows && c < n) ? to_f32<T>(w[r * n + c]) : 0.0f;
+    local = fmaxf(local, fabsf(v[k]));
+  }
+  const float amax = block_max(local, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+#pragma unroll
+  for (int k = 0; k < 64; ++k) {
+    const int idx = k * 256 + threadIdx.x;
+    const int64_t r = tr * 128 + idx / 128, c = tc * 128 + idx % 128;
+    if (r < rows && c < n) q[r * n + c] = trunc_sat(__fdiv_rn(v[k], s));
+  }
+  if (threadIdx.x == 0) scale[tr * nbc + tc] = s;
+}
+
+template <typename T, int MODE>
+int launch_quant_rows_T(const QArgs& a, int64_t rows, cudaStream_t st) {
+  const int nc = (a.n + 7) / 8;
+  const int cpt = (nc + QR_THREADS - 1) / QR_THREADS;
+  if (a.n % 8 != 0 || !a.vec) {
+    if (MODE != QI8_Q_TOKEN) return fail(QI8_EALIGN, "block quantization needs 16-byte aligned rows");
+    quant_rows_scalar_kernel<T><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
+    return check_cuda(cudaGetLastError(), "quant_rows_scalar_kernel launch");
+  }
+  switch (cpt) {
+#define QI8_CPT(c) case c: quant_rows_kernel<T, c, MODE><<<(unsigned)rows, QR_THREADS, 0, st>>>(a); break;
+    QI8_CPT(1) QI8_CPT(2)
+    case 3: QI8_CPT(4)
+    case 5: case 6: case 7: QI8_CPT(8)
+    case 9: case 10: case 11: case 12: case 13: case 14: case 15: QI8_CPT(16)
+#undef QI8_CPT
+    default:
+      if (MODE != QI8_Q_TOKEN) return fail(QI8_ESHAPE, "row width %d > 32768", a.n);
+      quant_rows_scalar_kernel<T><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
+  }
+  return check_cuda(cudaGetLastError(), "quant_rows_kernel launch");
+}
+
+template <int MODE>
+int launch_quant_rows(int dtype, const QArgs& a, int64_t rows, cudaStream_t st) {
+  switch (dtype) {
+    case QI8_BF16: return launch_quant_rows_T<__nv_bfloat16, MODE>(a, rows, st);
+    case QI8_F16: return launch_quant_rows_T<__half, MODE>(a, rows, st);
+    case QI8_F32: return launch_quant_rows_T<float, MODE>(a, rows, st);
+    default: return fail(QI8_EDTYPE, "input dtype %d not in {bf16, f16, f32}", dtype);
+  }
+}
+
+int grid_for(int64_t total, int threads) {
+  int64_t b = (total + threads - 1) / threads;
+  int64_t cap = (int64_t)sm_count() * 8;
+  if (cap <= 0) cap = 1184;
+  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+}  // namespace
+}  // namespace qi8
+
+using namespace qi8;
+
+extern "C" {
+
+int qi8_quant_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x, int mode,
+                   int block, int8_t* q_out, int64_t ld_q, float* scale_out, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(x && q_out && scale_out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(rows >= 0 && n > 0 && ld_x >= n && ld_q >= n, QI8_ESHAPE, "bad sizes rows=%lld n=%lld",
+              (long long)rows, (long long)n);
+  QI8_REQUIRE(n <= (1 << 30) && rows < (int64_t(1) << 31), QI8_ESHAPE, "sizes too large");
+  if (rows == 0) return QI8_OK;
+  const int es = elem_size(x_dtype);
+  QI8_REQUIRE(es == 2 || x_dtype == QI8_F32, QI8_EDTYPE, "input dtype %d not in {bf16, f16, f32}", x_dtype);
+  QArgs a{x, ld_x, (int)n, q_out, ld_q, scale_out, 0};
+  a.vec = aligned16(x) && (ld_x * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(q_out) & 7) == 0 && ld_q % 8 == 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mode == QI8_Q_TOKEN) return launch_quant_rows<QI8_Q_TOKEN>(x_dtype, a, rows, st);
+  if (mode == QI8_Q_BLOCK) {
+    QI8_REQUIRE(block == 128, QI8_ESHAPE, "block size must be 128 (got %d)", block);
+    QI8_REQUIRE(n % 128 == 0, QI8_ESHAPE, "Last dimension size must be divisible by block_size (block_size=128)");
+    return launch_quant_rows<QI8_Q_BLOCK>(x_dtype, a, rows, st);
+  }
+  return fail(QI8_EINVAL, "unknown quantization mode %d", mode);
+}
+
+int qi8_rotate_quant_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x,
+                          int64_t n_pad, const float* sign, int normalize, int mode, int8_t* q_out,
+                          float* scale_out, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(x && q_out && scale_out, QI8_EINVAL, "null pointer");
+  const int L = log2_exact(n_pad);
+  QI8_REQUIRE(L >= 1 && L <= 15, QI8_ESHAPE, "Hadamard size must be a power of 2 in [2, 32768], got %lld",
+              (long long)n_pad);
+  QI8_REQUIRE(n > 0 && n <= n_pad && ld_x >= n && rows >= 0 && rows < (int64_t(1) << 31), QI8_ESHAPE,
+              "bad sizes rows=%lld n=%lld n_pad=%lld", (long long)rows, (long long)n, (long long)n_pad);
+  QI8_REQUIRE(aligned16(q_out), QI8_EALIGN, "q_out must be 16-byte aligned");
+  if (rows == 0) return QI8_OK;
+  const int es = elem_size(x_dtype);
+  RotArgs a{};
+  a.x = x; a.ld_x = ld_x; a.n_in = (int)n; a.pre_sign = sign; a.post_sign = nullptr;
+  a.norm = (float)(1.0 / std::sqrt((double)n_pad)); a.do_norm = normalize != 0;
+  a.vec = aligned16(x) && (ld_x * es) % 16 == 0;
+  a.q = q_out; a.scale = scale_out;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mode == QI8_Q_TOKEN) return launch_rotate_dtype<RO_Q_TOKEN>(x_dtype, L, a, rows, st);
+  if (mode == QI8_Q_BLOCK) {
+    QI8_REQUIRE(n_pad >= 128, QI8_ESHAPE, "block mode needs n_pad >= 128");
+    return launch_rotate_dtype<RO_Q_BLOCK>(x_dtype, L, a, rows, st);
+  }
+  return fail(QI8_EINVAL, "unknown quantization mode %d", mode);
+}
+
+int qi8_fwht_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x, int64_t n_pad,
+                  const float* pre_sign, const float* post_sign, int normalize, float* out,
+                  void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(x && out, QI8_EINVAL, "null pointer");
+  const int L = log2_exact(n_pad);
+  QI8_REQUIRE(L >= 1 && L <= 15, QI8_ESHAPE, "Hadamard size must be a power of 2 in [2, 32768], got %lld",
+              (long long)n_pad);
+  QI8_REQUIRE(n > 0 && n <= n_pad && ld_x >= n && rows >= 0 && rows < (int64_t(1) << 31), QI8_ESHAPE,
+              "bad sizes");
+  QI8_REQUIRE(aligned16(out), QI8_EALIGN, "out must be 16-byte aligned");
+  if (rows == 0) return QI8_OK;
+  const int es = elem_size(x_dtype);
+  RotArgs a{};
+  a.x = x; a.ld_x = ld_x; a.n_in = (int)n; a.pre_sign = pre_sign; a.post_sign = post_sign;
+  a.norm = (float)(1.0 / std::sqrt((double)n_pad)); a.do_norm = normalize != 0;
+  a.vec = aligned16(x) && (ld_x * es) % 16 == 0;
+  a.f_out = out;
+  return launch_rotate_dtype<RO_F32>(x_dtype, L, a, rows, static_cast<cudaStream_t>(stream));
+}
+
+int qi8_unrotate_rows(const float* y_had, int64_t rows, int64_t n_pad, const float* sign_u,
+                      const void* bias, int bias_dtype, int64_t n_out, void* out, int out_dtype,
+                      int64_t ld_out, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(y_had && out, QI8_EINVAL, "null pointer");
+  const int L = log2_exact(n_pad);
+  QI8_REQUIRE(L >= 1 && L <= 15, QI8_ESHAPE, "Hadamard size must be a power of 2 in [2, 32768], got %lld",
+              (long long)n_pad);
+  QI8_REQUIRE(n_out > 0 && n_out <= n_pad && ld_out >= n_out && rows >= 0, QI8_ESHAPE, "bad sizes");
+  QI8_REQUIRE(out_dtype == QI8_BF16 || out_dtype == QI8_F16 || out_dtype == QI8_F32, QI8_EDTYPE,
+              "out dtype %d", out_dtype);
+  QI8_REQUIRE(!bias || bias_dtype == QI8_BF16 || bias_dtype == QI8_F16 || bias_dtype == QI8_F32, QI8_EDTYPE,
+              "bias dtype %d", bias_dtype);
+  if (rows == 0) return QI8_OK;
+  RotArgs a{};
+  a.x = y_had; a.ld_x = n_pad; a.n_in = (int)n_pad; a.pre_sign = nullptr; a.post_sign = sign_u;
+  a.norm = (float)(1.0 / std::sqrt((double)n_pad)); a.do_norm = 1;
+  a.vec = aligned16(y_had);
+  a.bias = bias; a.bias_dtype = bias_dtype; a.n_out = (int)n_out; a.out = out; a.out_dtype = out_dtype;
+  a.ld_out = ld_out;
+  return launch_rotate<float, RO_UNROT>(L, a, rows, static_cast<cudaStream_t>(stream));
+}
+
+int qi8_dequant(const int8_t* q, int64_t rows, int64_t n, const float* scale, int scale_kind, int block,
+                void* out, int out_dtype, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(q && scale && out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(rows >= 0 && n > 0, QI8_ESHAPE, "bad sizes");
+  QI8_REQUIRE(out_dtype == QI8_BF16 || out_dtype == QI8_F16 || out_dtype == QI8_F32, QI8_EDTYPE,
+              "out dtype %d", out_dtype);
+  QI8_REQUIRE(scale_kind >= QI8_S_SCALAR && scale_kind <= QI8_S_TILE128, QI8_EINVAL, "scale kind %d",
+              scale_kind);
+  if ((scale_kind == QI8_S_ROW_KBLOCK || scale_kind == QI8_S_TILE128))
+    QI8_REQUIRE(block > 0 && n % block == 0, QI8_ESHAPE, "n %% block != 0");
+  if (rows == 0) return QI8_OK;
+  const int64_t total = rows * n;
+  dequant_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, rows, n, scale, scale_kind, block, out, out_dtype);
+  return check_cuda(cudaGetLastError(), "dequant_kernel launch");
+}
+
+int qi8_quant_weight(const void* w, int w_dtype, int64_t rows, int64_t n, int scale_kind, int8_t* q_out,
+                     float* scale_out, void* workspace, int64_t workspace_bytes, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(w && q_out && scale_out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(rows > 0 && n > 0, QI8_ESHAPE, "bad sizes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t total = rows * n;
+  if (scale_kind == QI8_S_ROW) return qi8_quant_rows(w, w_dtype, rows, n, n, QI8_Q_TOKEN, 0, q_out, n, scale_out, stream);
+  if (scale_kind == QI8_S_SCALAR) {
+    QI8_REQUIRE(workspace && workspace_bytes >= 4, QI8_EINVAL, "tensorwise quantization needs a 4-byte workspace");
+    unsigned int* ws = static_cast<unsigned int*>(workspace);
+    QI8_CUDA(cudaMemsetAsync(ws, 0, 4, st));
+    const int g = grid_for(total, 256);
+    switch (w_dtype) {
+      case QI8_BF16:
+        absmax_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), total, ws);
+        quant_tensorwise_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), total, ws, q_out, scale_out);
+        break;
+      case QI8_F16:
+        absmax_kernel<__half><<<g, 256, 0, st>>>(static_cast<const __half*>(w), total, ws);
+        quant_tensorwise_kernel<__half><<<g, 256, 0, st>>>(static_cast<const __half*>(w), total, ws, q_out, scale_out);
+        break;
+      case QI8_F32:
+        absmax_kernel<float><<<g, 256, 0, st>>>(static_cast<const float*>(w), total, ws);
+        quant_tensorwise_kernel<float><<<g, 256, 0, st>>>(static_cast<const float*>(w), total, ws, q_out, scale_out);
+        break;
+      default: return fail(QI8_EDTYPE, "weight dtype %d", w_dtype);
+    }
+    return check_cuda(cudaGetLastError(), "tensorwise quant launch");
+  }
+  if (scale_kind == QI8_S_TILE128) {
+    QI8_REQUIRE(rows % 128 == 0 && n % 128 == 0, QI8_ESHAPE,
+                "Dimensions must be divisible by block_size=128, got shape (%lld, %lld)", (long long)rows, (long long)n);
+    dim3 grid((unsigned)(n / 128), (unsigned)(rows / 128));
+    switch (w_dtype) {
+      case QI8_BF16: quant_tile128_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), rows, n, q_out, scale_out); break;
+      case QI8_F16: quant_tile128_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w), rows, n, q_out, scale_out); break;
+      case QI8_F32: quant_tile128_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w), rows, n, q_out, scale_out); break;
+      default: return fail(QI8_EDTYPE, "weight dtype %d", w_dtype);
+    }
+    return check_cuda(cudaGetLastError(), "quant_tile128_kernel launch");
+  }
+  return fail(QI8_EINVAL, "scale kind %d not supported for weight quantization", scale_kind);
+}
+
+}  // extern "C"

@@ -1,0 +1,228 @@
+"""torch-facing wrappers of the libqi8 kernels.
+
+Outputs are allocated here with the PyTorch caching allocator (the C library
+never allocates); every launch goes on ``torch.cuda.current_stream()``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+
+
+def _next_pow2(n: int) -> int:
+    return 1 if n <= 1 else 1 << (n - 1).bit_length()
+
+
+def _rows2d(x: torch.Tensor) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _sign(s: Optional[torch.Tensor], n: int, device) -> Optional[torch.Tensor]:
+    if s is None:
+        return None
+    s = s.to(device=device, dtype=torch.float32).contiguous().reshape(-1)
+    assert s.numel() == n, f"sign vector has {s.numel()} entries, expected {n}"
+    return s
+
+
+def quant_rows(x: torch.Tensor, mode: int = L.QI8_Q_TOKEN, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-token (mode TOKEN) or per-128-block (mode BLOCK) int8 quantization of
+    the last dimension.  Returns ``(q int8 [..., n], scale fp32 [...] or [..., n/128])``."""
+    L.require_cuda(x)
+    x2 = _rows2d(x)
+    rows, n = x2.shape
+    q = torch.empty((rows, n), dtype=torch.int8, device=x.device)
+    ns = 1 if mode == L.QI8_Q_TOKEN else n // block
+    s = torch.empty((rows, ns), dtype=torch.float32, device=x.device)
+    lib = L.load()
+    L.check(lib.qi8_quant_rows(L.ptr(x2), L.dtype_code(x2.dtype), rows, n, x2.stride(0), mode, block,
+                               L.ptr(q), n, L.ptr(s), L.stream_ptr(x.device)), "qi8_quant_rows")
+    q = q.reshape(x.shape)
+    if mode == L.QI8_Q_TOKEN:
+        return q, s.reshape(*x.shape[:-1], 1)
+    return q, s.reshape(*x.shape[:-1], ns)
+
+
+def rotate_quant_rows(x: torch.Tensor, sign: Optional[torch.Tensor], n_pad: Optional[int] = None,
+                      normalize: bool = True, mode: int = L.QI8_Q_TOKEN) -> Tuple[torch.Tensor, torch.Tensor]:
+    """K1: ``quant(FWHT(pad(x, n_pad) * sign))``.  Returns ``(q [rows, n_pad], scale)``."""
+    L.require_cuda(x)
+    x2 = _rows2d(x)
+    rows, n = x2.shape
+    n_pad = n_pad or _next_pow2(n)
+    if n_pad & (n_pad - 1):
+        raise ValueError(f"Last dimension must be a power of 2, got {n_pad}")
+    q = torch.empty((rows, n_pad), dtype=torch.int8, device=x.device)
+    ns = 1 if mode == L.QI8_Q_TOKEN else n_pad // 128
+    s = torch.empty((rows, ns), dtype=torch.float32, device=x.device)
+    sg = _sign(sign, n_pad, x.device)
+    lib = L.load()
+    L.check(lib.qi8_rotate_quant_rows(L.ptr(x2), L.dtype_code(x2.dtype), rows, n, x2.stride(0), n_pad,
+                                      L.ptr(sg), int(normalize), mode, L.ptr(q), L.ptr(s),
+                                      L.stream_ptr(x.device)), "qi8_rotate_quant_rows")
+    return q, s
+
+
+def fwht_rows(x: torch.Tensor, n_pad: Optional[int] = None, pre_sign: Optional[torch.Tensor] = None,
+              post_sign: Optional[torch.Tensor] = None, normalize: bool = True,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FWHT of every row (last dim) to fp32 ``[..., n_pad]``."""
+    L.require_cuda(x)
+    x2 = _rows2d(x)
+    rows, n = x2.shape
+    n_pad = n_pad or n
+    if n_pad & (n_pad - 1) or n_pad < 1:
+        raise ValueError(f"Last dimension must be a power of 2, got {n_pad}")
+    if out is None:
+        out = torch.empty((rows, n_pad), dtype=torch.float32, device=x.device)
+    lib = L.load()
+    L.check(lib.qi8_fwht_rows(L.ptr(x2), L.dtype_code(x2.dtype), rows, n, x2.stride(0), n_pad,
+                              L.ptr(_sign(pre_sign, n_pad, x.device)), L.ptr(_sign(post_sign, n_pad, x.device)),
+                              int(normalize), L.ptr(out), L.stream_ptr(x.device)), "qi8_fwht_rows")
+    return out.reshape(*x.shape[:-1], n_pad)
+
+
+def unrotate_rows(y_had: torch.Tensor, sign_u: Optional[torch.Tensor], n_out: int,
+                  bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """K3: ``(FWHT(y_had) * sign_u)[:, :n_out] + bias`` -> ``out_dtype``."""
+    L.require_cuda(y_had)
+    assert y_had.dtype == torch.float32 and y_had.is_contiguous(), "y_had must be contiguous fp32"
+    rows, n_pad = y_had.reshape(-1, y_had.shape[-1]).shape
+    out = torch.empty((rows, n_out), dtype=out_dtype, device=y_had.device)
+    b = None if bias is None else bias.contiguous()
+    lib = L.load()
+    L.check(lib.qi8_unrotate_rows(L.ptr(y_had), rows, n_pad, L.ptr(_sign(sign_u, n_pad, y_had.device)),
+                                  L.ptr(b), L.dtype_code(b.dtype) if b is not None else 0, n_out, L.ptr(out),
+                                  L.dtype_code(out_dtype), n_out, L.stream_ptr(y_had.device)),
+            "qi8_unrotate_rows")
+    return out
+
+
+def scale_kind(scale: Optional[torch.Tensor], rows: int, K: int, is_weight: bool, block: int = 128) -> int:
+    """Classify a scale tensor for ``gemm_i8`` by its element count."""
+    if scale is None:
+        return L.QI8_S_NONE
+    n = scale.numel()
+    kb = K // block
+    if n == 1 and not (rows == 1 and kb == 1 and scale.dim() >= 2):
+        return L.QI8_S_SCALAR
+    if n == rows:
+        return L.QI8_S_ROW
+    if n == rows * kb:
+        return L.QI8_S_ROW_KBLOCK
+    if is_weight and n == ((rows + block - 1) // block) * kb:
+        return L.QI8_S_TILE128
+    raise AssertionError(f"cannot interpret scale of shape {tuple(scale.shape)} for rows={rows}, K={K}")
+
+
+def gemm_i8(a: torch.Tensor, b: torch.Tensor, a_scale: Optional[torch.Tensor] = None, a_kind: Optional[int] = None,
+            b_scale: Optional[torch.Tensor] = None, b_kind: Optional[int] = None,
+            bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
+            act: int = L.QI8_ACT_NONE, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """K2: ``a [M, K] int8 . b [N, K]^T int8`` with the fused epilogue."""
+    L.require_cuda(a, b)
+    assert a.dtype == torch.int8 and b.dtype == torch.int8, "int8 operands required"
+    a2 = a.reshape(-1, a.shape[-1])
+    assert a2.is_contiguous() and b.is_contiguous() and b.dim() == 2, "Input tensors must be contiguous"
+    M, K = a2.shape
+    N = b.shape[0]
+    assert b.shape[1] == K, f"Shape mismatch: b.shape={tuple(b.shape)}, expected [N, {K}]"
+    if a_scale is not None:
+        a_scale = a_scale.to(torch.float32).contiguous()
+        a_kind = scale_kind(a_scale, M, K, False) if a_kind is None else a_kind
+    else:
+        a_kind = L.QI8_S_NONE
+    if b_scale is not None:
+        b_scale = b_scale.to(torch.float32).contiguous()
+        b_kind = scale_kind(b_scale, N, K, True) if b_kind is None else b_kind
+    else:
+        b_kind = L.QI8_S_NONE
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    bb = None if bias is None else bias.contiguous()
+    lib = L.load()
+    L.check(lib.qi8_gemm_i8(L.ptr(a2), L.ptr(b), M, N, K, L.ptr(a_scale), a_kind, L.ptr(b_scale), b_kind,
+                            L.ptr(bb), L.dtype_code(bb.dtype) if bb is not None else 0, L.ptr(out),
+                            L.dtype_code(out.dtype), out.stride(0), act, L.stream_ptr(a.device)), "qi8_gemm_i8")
+    return out.reshape(*a.shape[:-1], N)
+
+
+def dequant(q: torch.Tensor, scale: torch.Tensor, kind: int, block: int = 128,
+            out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    L.require_cuda(q, scale)
+    q2 = q.reshape(-1, q.shape[-1]).contiguous()
+    rows, n = q2.shape
+    out = torch.empty((rows, n), dtype=out_dtype, device=q.device)
+    lib = L.load()
+    L.check(lib.qi8_dequant(L.ptr(q2), rows, n, L.ptr(scale.to(torch.float32).contiguous()), kind, block,
+                            L.ptr(out), L.dtype_code(out_dtype), L.stream_ptr(q.device)), "qi8_dequant")
+    return out.reshape(q.shape)
+
+
+def quant_weight(w: torch.Tensor, kind: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Tensorwise (SCALAR), per-row (ROW) or Triton-style 128x128 tile (TILE128) weight quantization."""
+    L.require_cuda(w)
+    w2 = w.reshape(-1, w.shape[-1]).contiguous()
+    rows, n = w2.shape
+    q = torch.empty((rows, n), dtype=torch.int8, device=w.device)
+    if kind == L.QI8_S_SCALAR:
+        s = torch.empty((), dtype=torch.float32, device=w.device)
+    elif kind == L.QI8_S_ROW:
+        s = torch.empty((rows, 1), dtype=torch.float32, device=w.device)
+    else:
+        s = torch.empty((rows // 128, n // 128), dtype=torch.float32, device=w.device)
+    ws = torch.empty(64, dtype=torch.uint8, device=w.device)
+    lib = L.load()
+    L.check(lib.qi8_quant_weight(L.ptr(w2), L.dtype_code(w2.dtype), rows, n, kind, L.ptr(q), L.ptr(s), L.ptr(ws),
+                                 ws.numel(), L.stream_ptr(w.device)), "qi8_quant_weight")
+    return q.reshape(w.shape), s
+
+
+def quip_workspace_bytes(M: int, N: int) -> int:
+    return int(L.load().qi8_quip_workspace_bytes(M, N))
+
+
+def quip_convert(w: torch.Tensor, s_u: torch.Tensor, s_v: torch.Tensor, store_transformed: bool = False,
+                 requant: int = L.QI8_REQ_ROW, block: int = 128, want_dequant: bool = True,
+                 workspace: Optional[torch.Tensor] = None):
+    """K4: QuIP Hadamard conversion of one weight.  Returns ``(q, scale, dequantized_weight or None)``."""
+    L.require_cuda(w)
+    assert w.dim() == 2, "weight must be 2-D"
+    w = w.contiguous()
+    M, N = w.shape
+    Mp, Np = _next_pow2(M), _next_pow2(N)
+    su = _sign(s_u, Mp, w.device)
+    sv = _sign(s_v, Np, w.device)
+    nbytes = quip_workspace_bytes(M, N)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+    if store_transformed:
+        q = torch.empty((Mp, Np), dtype=torch.int8, device=w.device)
+        s = torch.empty((Mp, 1), dtype=torch.float32, device=w.device)
+    else:
+        q = torch.empty((M, N), dtype=torch.int8, device=w.device)
+        if requant == L.QI8_REQ_BLOCK and N % block == 0:
+            s = torch.empty((M, N // block, 1), dtype=torch.float32, device=w.device)
+        elif requant == L.QI8_REQ_GLOBAL:
+            s = torch.empty((), dtype=torch.float32, device=w.device)
+        else:
+            s = torch.empty((M, 1), dtype=torch.float32, device=w.device)
+    deq = torch.empty((M, N), dtype=torch.float32, device=w.device) if want_dequant else None
+    lib = L.load()
+    L.check(lib.qi8_quip_convert(L.ptr(w), L.dtype_code(w.dtype), M, N, L.ptr(su), L.ptr(sv), int(store_transformed),
+                                 requant, block, L.ptr(q), L.ptr(s), L.ptr(deq), L.ptr(workspace), workspace.numel(),
+                                 L.stream_ptr(w.device)), "qi8_quip_convert")
+    return q, s, deq
+
+
+def device_status(reset: bool = True) -> None:
+    """Raise if a kernel's bounded wait expired since the last check."""
+    L.check(L.load().qi8_device_status(int(reset)), "device status")

@@ -1,0 +1,182 @@
+/*
+ * qi8.h -- C ABI of libqi8.so, the B200 (sm_100a) kernels behind the QuIP
+ * W8A8 quantized-linear path of convert_to_quant (ThunderFun/
+ * convert_to_quant_QuIP_INT8 v0.8.2).
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element counts and a cudaStream_t passed
+ *     as void* (NULL = legacy default stream); work is stream-ordered and the
+ *     call never synchronizes the host;
+ *   - never allocates or frees device memory (scratch is caller-provided);
+ *   - returns 0 (QI8_OK) or a negative qi8_status and records a message that
+ *     qi8_last_error() returns (thread-local).
+ *
+ * Matrices are row-major.  "ld" arguments are row strides in elements.
+ * Citations name the reference function (file:line inside the reference
+ * project) whose behaviour the entry point reproduces.
+ */
+#ifndef QI8_H_
+#define QI8_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QI8_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QI8_API __attribute__((visibility("default")))
+#else
+#define QI8_API
+#endif
+
+/* status codes */
+enum {
+  QI8_OK = 0,
+  QI8_EINVAL = -1,       /* null pointer / bad enum value */
+  QI8_ESHAPE = -2,       /* unsupported or inconsistent sizes */
+  QI8_EALIGN = -3,       /* pointer or stride misaligned for vector/TMA access */
+  QI8_EDTYPE = -4,       /* unsupported dtype combination */
+  QI8_ECUDA = -5,        /* a CUDA runtime/driver call failed */
+  QI8_ETIMEOUT = -6,     /* a kernel's bounded wait expired (device status word) */
+  QI8_EUNSUPPORTED = -7  /* no sm_100a device */
+};
+
+/* element types */
+enum { QI8_BF16 = 0, QI8_F16 = 1, QI8_F32 = 2, QI8_I8 = 3, QI8_I32 = 4 };
+
+/* activation / row quantization rules */
+enum {
+  /* per row: s = max(amax/127, 1e-30); q = rint(x * (1/s)) in [-128,127]
+     -- quantize_int8_axiswise, utils/float_utils.py:9-37 */
+  QI8_Q_TOKEN = 0,
+  /* per (row, 128-block): s = amax/127; q = trunc(x / s)
+     -- Triton act_quant, comfy/int8_kernels.py:72-123 */
+  QI8_Q_BLOCK = 1
+};
+
+/* GEMM scale kinds */
+enum {
+  QI8_S_NONE = 0,      /* scale 1 (no scale pointer)                          */
+  QI8_S_SCALAR = 1,    /* one value                       (tensorwise weight) */
+  QI8_S_ROW = 2,       /* one value per row of the operand (token / axis / QuIP [N,1]) */
+  QI8_S_ROW_KBLOCK = 3,/* [rows, K/128]: per row per 128-wide K block
+                          (comfy block act; QuIP block requant [N, K/128, 1]) */
+  QI8_S_TILE128 = 4    /* [rows/128, K/128]: per 128x128 weight tile (comfy block weight) */
+};
+
+/* GEMM epilogue activation */
+enum { QI8_ACT_NONE = 0, QI8_ACT_GELU = 1 };
+
+/* weight requantization schemes (converters/quip_int8.py:1614-1669) */
+enum { QI8_REQ_ROW = 0, QI8_REQ_GLOBAL = 1, QI8_REQ_BLOCK = 2 };
+
+QI8_API int qi8_version(void);
+QI8_API const char* qi8_last_error(void);
+/* 1 if device `device` is an sm_100 part this library was built for, else 0. */
+QI8_API int qi8_device_supported(int device);
+/* Reads (and with reset!=0 clears) the device status word that bounded
+   in-kernel waits set on expiry.  Returns QI8_OK, QI8_ETIMEOUT or QI8_ECUDA.
+   Synchronizes the current device. */
+QI8_API int qi8_device_status(int reset);
+
+/* Row quantization without rotation.
+   QI8_Q_TOKEN replaces quantize_int8_axiswise (utils/float_utils.py:9-37) as
+   called by optimized_linear (comfy/quant_ops.py:469); scale_out gets [rows].
+   QI8_Q_BLOCK replaces act_quant (comfy/int8_kernels.py:96-123); scale_out
+   gets [rows, n/block], block must be 128 (the reference default). */
+QI8_API int qi8_quant_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x,
+                   int mode, int block, int8_t* q_out, int64_t ld_q, float* scale_out,
+                   void* stream);
+
+/* K1: fused randomized FWHT + quantization of each row:
+     r = FWHT_{n_pad}(pad(x, n_pad) * sign) * (normalize ? 1/sqrt(n_pad) : 1)
+   then QI8_Q_TOKEN / QI8_Q_BLOCK quantization of r.  Replaces steps 1-2 of
+   quip_int8_matmul (comfy/int8_kernels.py:1424-1428, utils/hadamard.py:339-408)
+   followed by quantize_int8_axiswise.  n_pad is a power of two, 2 <= n_pad <=
+   32768, n <= n_pad (columns n..n_pad-1 are zero); sign may be NULL. */
+QI8_API int qi8_rotate_quant_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x,
+                          int64_t n_pad, const float* sign, int normalize, int mode,
+                          int8_t* q_out, float* scale_out, void* stream);
+
+/* FWHT of each row to fp32: out = FWHT(pad(x)*pre_sign)*norm*post_sign.
+   fast_hadamard_transform (utils/hadamard.py:339-408, comfy/hadamard_kernels.py:
+   244-373, 376-497); out is [rows, n_pad] with row stride n_pad; may alias x
+   when x is fp32 with ld_x == n_pad == n. */
+QI8_API int qi8_fwht_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t ld_x,
+                  int64_t n_pad, const float* pre_sign, const float* post_sign,
+                  int normalize, float* out, void* stream);
+
+/* K3: output un-rotation of a transformed-space linear:
+     y = (FWHT_{n_pad}(y_had) / sqrt(n_pad) * sign_u)[:, :n_out] + bias
+   (quip_int8_matmul steps 4-5, comfy/int8_kernels.py:1446-1450), written as
+   out_dtype (bf16 / f16 / f32) [rows, n_out] with row stride ld_out. */
+QI8_API int qi8_unrotate_rows(const float* y_had, int64_t rows, int64_t n_pad, const float* sign_u,
+                      const void* bias, int bias_dtype, int64_t n_out, void* out,
+                      int out_dtype, int64_t ld_out, void* stream);
+
+/* K2: D[M,N] = A[M,K] (int8) x B[N,K]^T (int8) on tcgen05 tensor cores with a
+   fused epilogue, TMA-fed, TMEM accumulators.
+   - No block scale kinds: exact int32 accumulation over all of K, then
+     out = acc (QI8_I32 output; scales must be NONE) or
+     out = float(acc) * (sa[m] * sb[n]) + bias[n]   -> out_dtype
+     exactly as optimized_linear (comfy/quant_ops.py:471-474) / mm_8bit
+     (comfy/int8_matmul_kernels.py:82-110).
+   - QI8_S_ROW_KBLOCK / QI8_S_TILE128 on either side: per-128-K-block
+     promotion acc += float(acc_kb) * sa(m,kb) * sb(n,kb), as int8_gemm /
+     int8_addmm (comfy/int8_kernels.py:335-647); row-constant scales are
+     applied once at the end.
+   A, B: 16-byte aligned, K % 16 == 0 (TMA row pitch); N % 16 == 0;
+   block kinds need K % 128 == 0.  act: QI8_ACT_GELU applies exact-erf GELU
+   to the bias-added value (bf16-rounded first when out_dtype is bf16).
+   ld_out: row stride of out (>= N). */
+QI8_API int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K,
+                const float* a_scale, int a_kind, const float* b_scale, int b_kind,
+                const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ld_out,
+                int act, void* stream);
+
+/* Dequantize int8 rows/tiles: out = q * scale.
+   scale_kind QI8_S_SCALAR / QI8_S_ROW (TensorWise / AxisWise dequantize,
+   comfy/quant_ops.py:326-339), QI8_S_ROW_KBLOCK with block (act_dequant,
+   comfy/int8_kernels.py:126-179), QI8_S_TILE128 (weight_dequant,
+   comfy/int8_kernels.py:256-330). */
+QI8_API int qi8_dequant(const int8_t* q, int64_t rows, int64_t n, const float* scale, int scale_kind,
+                int block, void* out, int out_dtype, void* stream);
+
+/* Weight quantization (no rotation).
+   QI8_S_SCALAR: quantize_int8_tensorwise (utils/float_utils.py:40-66),
+     needs workspace of >= 4 bytes (global absmax); scale_out [1].
+   QI8_S_ROW:    quantize_int8_axiswise per row; scale_out [rows].
+   QI8_S_TILE128: Triton weight_quant (comfy/int8_kernels.py:182-253):
+     s = max(amax/127, 1e-8), trunc; scale_out [rows/128, n/128]. */
+QI8_API int qi8_quant_weight(const void* w, int w_dtype, int64_t rows, int64_t n, int scale_kind,
+                     int8_t* q_out, float* scale_out, void* workspace, int64_t workspace_bytes,
+                     void* stream);
+
+/* K4: offline QuIP Hadamard conversion of one weight W[M,N] (identity Hessian:
+   the LDLQ step reduces to rotated-space RTN):
+     W' = FHT_N(FHT_M(pad(W) * s_u * s_v^T)),  s' = max(rowamax(W')/127, 1e-12),
+     Q' = rint(W'/s') in [-127,127],  W_d = slice(FHT_M(FHT_N(Q' s')) * s_u * s_v)
+   (converters/quip_int8.py:539-551, 1272-1274, 655, 1452, 1489-1506), then
+   - store_transformed != 0: q_out = Q' [M_pad, N_pad], scale_out = s' [M_pad]
+     (quip_int8.py:1558-1608);
+   - else requant W_d (quip_int8.py:1614-1669): QI8_REQ_ROW -> scale [M],
+     QI8_REQ_GLOBAL -> scale [1], QI8_REQ_BLOCK -> scale [M, N/block]
+     (falls back to QI8_REQ_ROW when N % block != 0, as the reference does);
+     q_out = Q [M, N].
+   dequant_out (optional, fp32 [M,N]) receives W_d.  s_u [M_pad], s_v [N_pad]
+   are +-1 fp32 with M_pad = next_pow2(M), N_pad = next_pow2(N), both <= 32768.
+   workspace: >= qi8_quip_workspace_bytes(M, N) bytes, 256-byte aligned. */
+QI8_API int64_t qi8_quip_workspace_bytes(int64_t M, int64_t N);
+QI8_API int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, const float* s_u,
+                     const float* s_v, int store_transformed, int requant, int block,
+                     int8_t* q_out, float* scale_out, float* dequant_out, void* workspace,
+                     int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QI8_H_ */
