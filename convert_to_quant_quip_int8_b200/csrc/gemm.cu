@@ -51,6 +51,13 @@ constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) +
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;  // 0.2 s when cleaning up
 
+// Block-scaled mode keeps every TMEM accumulator pre-loaded with the int32
+// bit pattern of 1.5*2^23 and always accumulates onto it: after the K block,
+// the bits read back are exactly the fp32 value 1.5*2^23 + partial (partial
+// magnitude <= 128*128*128 < 2^22), so one fp32 subtract recovers it.
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;
+constexpr float MAGIC_F = 12582912.0f;
+
 // instruction descriptor: D s32, A/B signed int8, both K-major, N=256, M=128
 constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                            ((uint32_t)(BM >> 4) << 24);
@@ -161,6 +168,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Writes the same 32-bit value v into 16 consecutive columns of this warp's lanes.
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
 // 128 bytes, 8-row core groups 1024 bytes apart (SBO), sm_100 version bit.
@@ -234,6 +258,49 @@ __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, co
   }
 }
 
+// Stores 8 consecutive fp32 results of row m starting at column n0 (n0 % 8 == 0).
+__device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, const float (&y)[8]) {
+  const int64_t off = (int64_t)m * p.ld_out + n0;
+  const bool full = (n0 + 8 <= p.N);
+  if (p.out_dtype == QI8_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + off;
+    if (full) {
+      uint4 u;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+      *reinterpret_cast<uint4*>(o) = u;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = __float2bfloat16_rn(y[j]);
+    }
+  } else if (p.out_dtype == QI8_F16) {
+    __half* o = static_cast<__half*>(p.out) + off;
+    if (full) {
+      uint4 u;
+      __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+      *reinterpret_cast<uint4*>(o) = u;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = __float2half_rn(y[j]);
+    }
+  } else {
+    float* o = static_cast<float*>(p.out) + off;
+    if (full) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = y[j];
+    }
+  }
+}
+
 __device__ __forceinline__ void store_row32_i32(const GemmArgs& p, int m, int n0, const uint32_t (&r)[32]) {
   int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)m * p.ld_out + n0;
   if (n0 + 32 <= p.N) {
@@ -253,7 +320,7 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
 }
 
 template <bool PROMOTE>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -302,6 +369,20 @@ __global__ void __maxnreg__(200)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int KB = p.KB;
+  if constexpr (PROMOTE) {
+    if (warp < NUM_EPI_WARPS) {
+      // pre-bias both accumulator buffers (this warp's lanes and columns)
+      const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tmem_fill16(tmem_base + lb + (uint32_t)(b * BN + (warp >> 2) * 128 + c * 16), MAGIC_BITS);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
 
   if (warp == PRODUCER_WARP) {
     if (lane == 0) {
@@ -361,7 +442,8 @@ __global__ void __maxnreg__(200)
             const uint64_t db = sw128_desc(sB + s * B_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 32; ++k)
-              tc_mma_i8(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), (kb > kb0 || k > 0) ? 1u : 0u);
+              tc_mma_i8(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k),
+                        (PROMOTE || kb > kb0 || k > 0) ? 1u : 0u);
             tc_commit(empty_bar(s));
             if (++s == STAGES) {
               s = 0;
@@ -416,49 +498,47 @@ __global__ void __maxnreg__(200)
           }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + c * 32), r);
+          for (int c = 0; c < 8; ++c) {
+            uint32_t r[16];
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + c * 16);
+            tmem_ld16(ta, r);
             tmem_wait_ld();
-            if (c == 3) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(tempty_bar(buf));
-            }
+            tmem_fill16(ta, MAGIC_BITS);  // re-bias for this buffer's next K block
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              // exact int32 -> fp32 for |x| < 2^22: bits(0x4B400000 + x) - 1.5*2^23
-              float2 f = make_float2(__int_as_float((int)(r[2 * j] + 0x4B400000u)),
-                                     __int_as_float((int)(r[2 * j + 1] + 0x4B400000u)));
-              f = __fadd2_rn(f, make_float2(-12582912.0f, -12582912.0f));
+            for (int j = 0; j < 8; ++j) {
+              float2 f = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
               float2 sc;
               if (b_col) {
-                sc = *reinterpret_cast<const float2*>(my_sc + c * 32 + 2 * j);
+                sc = *reinterpret_cast<const float2*>(my_sc + c * 16 + 2 * j);
                 if (a_kb) sc = __fmul2_rn(sc, make_float2(sa, sa));
               } else {
                 sc = make_float2(sconst, sconst);
               }
-              acc[c * 16 + j] = __ffma2_rn(f, sc, acc[c * 16 + j]);
+              acc[c * 8 + j] = __ffma2_rn(f, sc, acc[c * 8 + j]);
             }
           }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar(buf));
         }
         if (!ok) break;
         if (row_ok && cols_ok) {
           const float fa = row_scale(p.a_scale, p.a_kind, m);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int n0 = ncol0 + c * 32;
-            if (n0 >= p.N) break;
-            float y[32];
+          for (int g = 0; g < 16; ++g) {
+            const int n0 = ncol0 + g * 8;
+            if (n0 < p.N) {
+              float y[8];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j;
-              const float v = (j & 1) ? acc[c * 16 + (j >> 1)].y : acc[c * 16 + (j >> 1)].x;
-              float fb = 1.0f;
-              if (n < p.N) fb = row_scale(p.b_scale, p.b_kind, n);
-              y[j] = n < p.N ? finish_value(__fmul_rn(__fmul_rn(v, fa), fb), n, p) : 0.0f;
+              for (int j = 0; j < 8; ++j) {
+                const int n = n0 + j < p.N ? n0 + j : p.N - 1;
+                const float v = (j & 1) ? acc[g * 4 + (j >> 1)].y : acc[g * 4 + (j >> 1)].x;
+                y[j] = finish_value(__fmul_rn(__fmul_rn(v, fa), row_scale(p.b_scale, p.b_kind, n)), n, p);
+              }
+              store_row8(p, m, n0, y);
             }
-            store_row32(p, m, n0, y);
           }
         }
       } else {
@@ -602,5 +682,12 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = p.num_tiles < sms ? p.num_tiles : sms;
   kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mapA, mapB, p);
-  return check_cuda(cudaGetLastError(), "gemm_i8_kernel launch");
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, kern);
+    return fail(QI8_ECUDA, "gemm_i8_kernel launch: %s (regs=%d maxThreads=%d local=%zu smem=%d grid=%d)",
+                cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes, SMEM_BYTES, grid);
+  }
+  return QI8_OK;
 }
