@@ -1,0 +1,378 @@
+"""Benchmark of the QuIP W8A8 quantized-linear path on B200.
+
+Workload (one step): the DiT MLP pair with block-128 K scales --
+x [4096, 3072] bf16 -> per-token int8 (K1) -> W1 [12288, 3072] int8 GEMM with
+per-128-K-block promotion + GELU epilogue (K2) -> per-token int8 (K1) ->
+W2 [3072, 12288] int8 GEMM (K2) -> bf16 [4096, 3072].
+Metric: W8A8 linear TOPS (2 * M * N * K per GEMM, both GEMMs), whole job.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this framework
+    python bench.py --impl reference [...]                     # CPU reference arm
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of
+the workload (weak scaling, no collective on the data path); the time is
+the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = ("dit_mlp_pair_block128: x[4096,3072] bf16 -> W1[12288,3072] int8 (QuIP-rotated, block-128 requant "
+            "[12288,24,1]) + GELU -> W2[3072,12288] int8 (block-128 requant) -> bf16")
+METRIC = "W8A8 QuIP linear TOPS (DiT MLP pair, block-128 K scales)"
+UNIT = "TOPS"
+L2_NOTE = "inputs larger than L2: per-step footprint ~280 MB (x 25 MB, W1+W2 75 MB, h 100 MB + 50 MB, y 25 MB) > 126 MB"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="qi8", choices=["qi8", "reference"])
+    ap.add_argument("--cpu-tokens", type=int, default=512, help="token sample of the CPU baseline step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- peaks
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ------------------------------------------------------------ clock probe
+class ClockProbe:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.idx = device_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower().startswith("active")})
+        sm = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------- distributed
+def dist_init(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world <= 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ CPU arm
+def cpu_reference_step_fn(tokens: int):
+    """One step of the CPU oracle port (numpy) on a `tokens`-row sample of the
+    workload; returns (callable, ops per call, description)."""
+    import oracle as O
+    from convert_to_quant_quip_int8_b200.workloads import DitMlpPair
+
+    wl = DitMlpPair()
+    x = wl.activations()[:tokens].float().numpy()
+    # weights: block-128 requant of the same seeded tensors (the offline
+    # rotation of W1 is conversion-time work and does not change the timed step)
+    q1, s1 = O.quip_requant(wl.w1().float().numpy(), "block", True)
+    q2, s2 = O.quip_requant(wl.w2().float().numpy(), "block", True)
+    s1 = s1.reshape(q1.shape[0], -1)
+    s2 = s2.reshape(q2.shape[0], -1)
+
+    def step():
+        xq, xs = O.quantize_int8_axiswise(x)
+        h = O.int8_gemm_block(xq, np.ones((tokens, 1), np.float32), q1, s1, None, b_layout="row") * xs
+        h = O.round_bf16(O.gelu_f32(O.round_bf16(h)))
+        hq, hs = O.quantize_int8_axiswise(h)
+        y = O.int8_gemm_block(hq, np.ones((tokens, 1), np.float32), q2, s2, None, b_layout="row") * hs
+        return O.f32_to_bf16(y)
+
+    return step, wl.ops_per_step(tokens), f"{tokens} of 4096 tokens through both linears (numpy oracle port)"
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_cpu(tokens: int, steps: int, warmup: int):
+    step, ops, sample = cpu_reference_step_fn(tokens)
+    for _ in range(max(0, warmup)):
+        step()
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return ops / med / 1e12, med, sample
+
+
+# ------------------------------------------------------------- GPU arm
+def build_model(device):
+    from convert_to_quant_quip_int8_b200 import _lib as L
+    from convert_to_quant_quip_int8_b200 import ops
+    from convert_to_quant_quip_int8_b200.workloads import DitMlpPair
+
+    wl = DitMlpPair()
+    x = wl.activations()
+    su, sv = wl.w1_signs()
+    w1 = wl.w1().to(device)
+    q1, s1, _ = ops.quip_convert(w1, su, sv, requant=L.QI8_REQ_BLOCK, want_dequant=False)
+    del w1
+    w2 = wl.w2().to(device)
+    q2, s2 = ops.requant_weight(w2, L.QI8_REQ_BLOCK)
+    del w2
+    torch.cuda.synchronize(device)
+    return wl, x, (q1, s1.reshape(q1.shape[0], -1).contiguous()), (q2, s2.reshape(q2.shape[0], -1).contiguous())
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return main_reference(args)
+    from convert_to_quant_quip_int8_b200 import _lib as L
+    from convert_to_quant_quip_int8_b200 import ops
+    from convert_to_quant_quip_int8_b200.comfy.quant_ops import QuantizedTensor
+
+    rank, world, local = dist_init(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl, x_cpu, (q1, s1), (q2, s2) = build_model(device)
+    T, H, F_ = wl.tokens, wl.hidden, wl.ffn
+    x = x_cpu.to(device)
+    stream = torch.cuda.current_stream(device)
+
+    # preallocated activations
+    xq = torch.empty((T, H), dtype=torch.int8, device=device)
+    h = torch.empty((T, F_), dtype=torch.bfloat16, device=device)
+    y = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+    lib = L.load()
+    sp = L.stream_ptr(device)
+
+    def k1(src, n, dst_q, dst_s):
+        L.check(lib.qi8_quant_rows(L.ptr(src), L.QI8_BF16, T, n, n, L.QI8_Q_TOKEN, 128, L.ptr(dst_q), n,
+                                   L.ptr(dst_s), sp))
+
+    xs = torch.empty((T, 1), dtype=torch.float32, device=device)
+    hq = torch.empty((T, F_), dtype=torch.int8, device=device)
+    hs = torch.empty((T, 1), dtype=torch.float32, device=device)
+
+    def gemm(a, a_s, b, b_s, out, act):
+        M, K = a.shape
+        N = b.shape[0]
+        L.check(lib.qi8_gemm_i8(L.ptr(a), L.ptr(b), M, N, K, L.ptr(a_s), L.QI8_S_ROW, L.ptr(b_s),
+                                L.QI8_S_ROW_KBLOCK, None, 0, L.ptr(out), L.QI8_BF16, N, act, sp))
+
+    def step(ev=None):
+        k1(x, H, xq, xs)
+        if ev:
+            ev[0].record(stream)
+        gemm(xq, xs, q1, s1, h, L.QI8_ACT_GELU)
+        if ev:
+            ev[1].record(stream)
+        k1(h, F_, hq, hs)
+        if ev:
+            ev[2].record(stream)
+        gemm(hq, hs, q2, s2, y, L.QI8_ACT_NONE)
+        if ev:
+            ev[3].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    ops.device_status()
+
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches_per_step = 4
+    # per-step events around the two GEMMs, all on the launching stream
+    gemm_ms = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    with ClockProbe(device.index if device.index is not None else 0) as probe:
+        barrier(world)
+        torch.cuda.synchronize(device)
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(gemm_ms[i])
+        t_end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+    ops.device_status()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    elapsed_ms = max_over_ranks(elapsed_ms, world, device)
+    g1 = [e[0].elapsed_time(e[1]) for e in gemm_ms]
+    g2 = [e[2].elapsed_time(e[3]) for e in gemm_ms]
+    ops_step = wl.ops_per_step()
+    value = world * ops_step * args.steps / (elapsed_ms / 1e3) / 1e12
+    ms_per_step = elapsed_ms / args.steps
+
+    # ---- e2e through the public API: host pinned x -> F.linear -> GELU -> F.linear -> host
+    w1_qt = QuantizedTensor(q1, "BlockWiseINT8Layout", {"scale": s1.reshape(F_, -1, 1), "block_size": 128,
+                                                        "is_weight": True, "orig_dtype": torch.bfloat16})
+    w2_qt = QuantizedTensor(q2, "BlockWiseINT8Layout", {"scale": s2.reshape(H, -1, 1), "block_size": 128,
+                                                        "is_weight": True, "orig_dtype": torch.bfloat16})
+    x_host = x_cpu.pin_memory()
+    y_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        hd = torch.nn.functional.gelu(torch.nn.functional.linear(xd, w1_qt))
+        yd = torch.nn.functional.linear(hd, w2_qt)
+        y_host.copy_(yd, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e_steps = max(3, min(args.steps, 10))
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device) / e_steps
+    e2e_value = world * ops_step / (e2e_ms / 1e3) / 1e12
+    # parity spot check of the timed path against the public-API path
+    ref_y = y.float()
+    rel = float((y_host.to(device).float() - ref_y).norm() / ref_y.norm().clamp_min(1e-30))
+
+    if rank != 0:
+        _finish(world)
+        return
+
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    gemm_ops = 2 * T * H * F_
+    g_avg_ms = statistics.mean(g1 + g2)
+    achieved = gemm_ops / (g_avg_ms / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (fp32 promote, bf16 out)",
+        "data": "synthetic (seeded N(0,1) activations with 0.5% x30 outlier channels; N(0,0.02) weights)",
+        "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F_, "block": 128,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single", "l2": L2_NOTE},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(T * H * 2),
+                "d2h_bytes_per_step": int(T * H * 2), "ms_per_step": round(e2e_ms, 4),
+                "path": "F.linear(x, QuantizedTensor W1) -> F.gelu -> F.linear(., W2), pinned host in/out",
+                "rel_err_vs_device_path": rel},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": None,
+                     "kernel": "gemm_i8_kernel<PROMOTE> (both GEMMs, CUDA events on the launch stream)",
+                     "peak_note": f"dense int8 = 2 x {peak_kind} cuBLAS bf16 burst ({peaks.get('bf16_tflops')} TF/s)",
+                     "per_gemm_ms": {"w1_gelu": round(statistics.mean(g1), 4), "w2": round(statistics.mean(g2), 4)}},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": probe.summary(),
+    }
+    if not args.no_cpu_baseline and world == 1:
+        torch.set_num_threads(cpu_cores())
+        cv, cmed, sample = run_cpu(args.cpu_tokens, 2, 1)
+        line["cpu_baseline"] = {"value": round(cv, 4), "unit": UNIT, "cores": cpu_cores(), "kind": "port",
+                                "sample": sample, "s_per_step": round(cmed, 3)}
+    print(json.dumps(line), flush=True)
+    _finish(world)
+
+
+def _finish(world):
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    tokens = args.cpu_tokens
+    value, med, sample = run_cpu(tokens, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x int8 -> int32 (fp32 promote, bf16 out)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": 4096, "hidden": 3072, "ffn": 12288, "block": 128,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -53,12 +53,14 @@ SIGNATURES = {
     "qi8_quant_rows": (_I, [_P, _I, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
     "qi8_rotate_quant_rows": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _I, _I, _P, _P, _P]),
     "qi8_fwht_rows": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P]),
+    "qi8_fwht_cols": (_I, [_P, _I64, _I64, _I64, _I, ctypes.c_float, _P]),
     "qi8_unrotate_rows": (_I, [_P, _I64, _I64, _P, _P, _I, _I64, _P, _I, _I64, _P]),
     "qi8_gemm_i8": (_I, [_P, _P, _I64, _I64, _I64, _P, _I, _P, _I, _P, _I, _P, _I, _I64, _I, _P]),
     "qi8_dequant": (_I, [_P, _I64, _I64, _P, _I, _I, _P, _I, _P]),
     "qi8_quant_weight": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _P, _I64, _P]),
     "qi8_quip_workspace_bytes": (_I64, [_I64, _I64]),
     "qi8_quip_convert": (_I, [_P, _I, _I64, _I64, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I64, _P]),
+    "qi8_requant_weight": (_I, [_P, _I, _I64, _I64, _I64, _I, _I, _P, _P, _P, _I64, _P]),
 }
 
 _lib = None

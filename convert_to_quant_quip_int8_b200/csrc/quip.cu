@@ -38,12 +38,15 @@ struct ColArgs {
   const float* s_u;
   const float* s_v;
   int b0, rbits;  // this pass transforms row-index bits [b0, b0 + rbits)
-  float norm;
+  float norm;     // last pass: multiply by norm (FINAL_MUL) or divide by it (FINAL_DIV)
+  int64_t ld_x;   // row stride of x (columns j < N_pad are transformed)
   float* dst;  // inverse last pass: W_d destination [M, N] with row stride ld_dst
   int64_t ld_dst;
 };
 
-template <bool LOAD_W, bool NORM, bool SIGN_OUT>
+enum { FINAL_NONE = 0, FINAL_MUL = 1, FINAL_DIV = 2 };
+
+template <bool LOAD_W, int FINAL, bool SIGN_OUT>
 __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
   extern __shared__ float tile[];  // [R][COL_STRIP]
   const int R = 1 << a.rbits;
@@ -64,7 +67,7 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
         v = __fmul_rn(v, __ldg(a.s_u + i));
         v = __fmul_rn(v, __ldg(a.s_v + j));
       } else {
-        v = a.x[i * a.N_pad + j];
+        v = a.x[i * a.ld_x + j];
       }
     }
     tile[k * COL_STRIP + lane] = v;
@@ -83,7 +86,8 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
   for (int k = warp; k < R; k += NW) {
     const int64_t i = hi_base + ((int64_t)k << a.b0);
     float v = tile[k * COL_STRIP + lane];
-    if constexpr (NORM) v = __fmul_rn(v, a.norm);
+    if constexpr (FINAL == FINAL_MUL) v = __fmul_rn(v, a.norm);
+    if constexpr (FINAL == FINAL_DIV) v = __fdiv_rn(v, a.norm);
     if constexpr (SIGN_OUT) {
       if (i < a.M && j < a.N) {
         v = __fmul_rn(v, __ldg(a.s_u + i));
@@ -91,7 +95,7 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
         a.dst[i * a.ld_dst + j] = v;
       }
     } else {
-      if (col_ok) a.x[i * a.N_pad + j] = v;
+      if (col_ok) a.x[i * a.ld_x + j] = v;
     }
   }
 }
@@ -169,7 +173,8 @@ int launch_row(int L, const RowArgs& a, int64_t rows, cudaStream_t st) {
 
 // ------------------------------------------------------------- requant
 struct ReqArgs {
-  const float* w;
+  const void* w;
+  int w_dtype;
   int64_t ld_w, M, N;
   int8_t* q;
   float* scale;
@@ -180,13 +185,13 @@ struct ReqArgs {
 __global__ void __launch_bounds__(256) requant_row_kernel(ReqArgs a) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
-  const float* wr = a.w + row * a.ld_w;
+  const int64_t r0 = row * a.ld_w;
   float local = 0.0f;
-  for (int64_t c = threadIdx.x; c < a.N; c += blockDim.x) local = fmaxf(local, fabsf(wr[c]));
+  for (int64_t c = threadIdx.x; c < a.N; c += blockDim.x) local = fmaxf(local, fabsf(load_as_f32(a.w, a.w_dtype, r0 + c)));
   const float amax = block_max(local, red);
   const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
   for (int64_t c = threadIdx.x; c < a.N; c += blockDim.x)
-    a.q[row * a.N + c] = rint_clamp(__fdiv_rn(wr[c], s), -127.0f, 127.0f);
+    a.q[row * a.N + c] = rint_clamp(__fdiv_rn(load_as_f32(a.w, a.w_dtype, r0 + c), s), -127.0f, 127.0f);
   if (threadIdx.x == 0) a.scale[row] = s;
 }
 
@@ -195,13 +200,13 @@ __global__ void __launch_bounds__(256) requant_block_kernel(ReqArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int per = a.block / 32;  // 1, 2 or 4
   const int64_t nb = a.N / a.block;
-  const float* wr = a.w + row * a.ld_w;
+  const int64_t r0 = row * a.ld_w;
   for (int64_t b = warp; b < nb; b += 8) {
     float v[4];
     float m = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      v[k] = k < per ? wr[b * a.block + k * 32 + lane] : 0.0f;
+      v[k] = k < per ? load_as_f32(a.w, a.w_dtype, r0 + b * a.block + k * 32 + lane) : 0.0f;
       m = fmaxf(m, fabsf(v[k]));
     }
     m = warp_max(m);
@@ -213,13 +218,12 @@ __global__ void __launch_bounds__(256) requant_block_kernel(ReqArgs a) {
   }
 }
 
-__global__ void absmax_rows_kernel(const float* __restrict__ w, int64_t ld_w, int64_t M, int64_t N,
-                                   unsigned int* __restrict__ out) {
+__global__ void absmax_rows_kernel(ReqArgs a, unsigned int* __restrict__ out) {
   float m = 0.0f;
-  const int64_t total = M * N;
+  const int64_t total = a.M * a.N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / N, c = i - r * N;
-    m = fmaxf(m, fabsf(w[r * ld_w + c]));
+    const int64_t r = i / a.N, c = i - r * a.N;
+    m = fmaxf(m, fabsf(load_as_f32(a.w, a.w_dtype, r * a.ld_w + c)));
   }
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
@@ -231,8 +235,24 @@ __global__ void requant_global_kernel(ReqArgs a) {
   const int64_t total = a.M * a.N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / a.N, c = i - r * a.N;
-    a.q[i] = rint_clamp(__fdiv_rn(a.w[r * a.ld_w + c], s), -127.0f, 127.0f);
+    a.q[i] = rint_clamp(__fdiv_rn(load_as_f32(a.w, a.w_dtype, r * a.ld_w + c), s), -127.0f, 127.0f);
   }
+}
+
+int launch_requant(ReqArgs qa, int requant, cudaStream_t st) {
+  if (requant == QI8_REQ_BLOCK && qa.N % qa.block != 0) requant = QI8_REQ_ROW;
+  if (requant == QI8_REQ_ROW) {
+    requant_row_kernel<<<(unsigned)qa.M, 256, 0, st>>>(qa);
+  } else if (requant == QI8_REQ_BLOCK) {
+    requant_block_kernel<<<(unsigned)qa.M, 256, 0, st>>>(qa);
+  } else {
+    unsigned int* gword = const_cast<unsigned int*>(qa.gmax);
+    QI8_CUDA(cudaMemsetAsync(gword, 0, 4, st));
+    const int sms = sm_count() > 0 ? sm_count() : 148;
+    absmax_rows_kernel<<<sms * 4, 256, 0, st>>>(qa, gword);
+    requant_global_kernel<<<sms * 4, 256, 0, st>>>(qa);
+  }
+  return check_cuda(cudaGetLastError(), "requant launch");
 }
 
 int64_t next_pow2(int64_t n) {
@@ -242,7 +262,10 @@ int64_t next_pow2(int64_t n) {
 }
 
 // Runs the M-direction transform over X in passes of <= COL_MAX_BITS bits.
-int col_passes(bool forward, const ColArgs& base, cudaStream_t st) {
+// forward: the first pass loads W (signs, zero padding); backward: the last
+// pass applies the signs and writes the sliced result to dst.  `final`
+// selects the normalization of the last pass.
+int col_passes(bool forward, const ColArgs& base, cudaStream_t st, int final = FINAL_MUL) {
   const int L = log2_exact(base.M_pad);
   int b0 = 0;
   while (b0 < L || (L == 0 && b0 == 0)) {
@@ -253,14 +276,18 @@ int col_passes(bool forward, const ColArgs& base, cudaStream_t st) {
     const bool first = (b0 == 0), last = (b0 + rb == L);
     const size_t smem = sizeof(float) * COL_STRIP * ((size_t)1 << rb);
     dim3 grid((unsigned)((base.N_pad + COL_STRIP - 1) / COL_STRIP), (unsigned)(base.M_pad >> rb));
-    void (*kern)(ColArgs) = nullptr;
-    if (forward) {
-      if (first && last) kern = col_fwht_kernel<true, true, false>;
-      else if (first) kern = col_fwht_kernel<true, false, false>;
-      else if (last) kern = col_fwht_kernel<false, true, false>;
-      else kern = col_fwht_kernel<false, false, false>;
-    } else {
-      kern = last ? col_fwht_kernel<false, true, true> : col_fwht_kernel<false, false, false>;
+    void (*kern)(ColArgs) = col_fwht_kernel<false, FINAL_NONE, false>;
+    if (forward == true && base.w != nullptr) {
+      if (first && last) kern = col_fwht_kernel<true, FINAL_MUL, false>;
+      else if (first) kern = col_fwht_kernel<true, FINAL_NONE, false>;
+      else if (last) kern = col_fwht_kernel<false, FINAL_MUL, false>;
+    } else if (forward) {  // in-place transform of x (no signs)
+      if (last) {
+        if (final == FINAL_MUL) kern = col_fwht_kernel<false, FINAL_MUL, false>;
+        else if (final == FINAL_DIV) kern = col_fwht_kernel<false, FINAL_DIV, false>;
+      }
+    } else if (last) {
+      kern = col_fwht_kernel<false, FINAL_MUL, true>;
     }
     if (smem > 48 * 1024) QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<grid, COL_THREADS, smem, st>>>(a);
@@ -277,6 +304,20 @@ int col_passes(bool forward, const ColArgs& base, cudaStream_t st) {
 using namespace qi8;
 
 extern "C" {
+
+int qi8_fwht_cols(float* x, int64_t rows, int64_t cols, int64_t ld, int final_mode, float factor, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(x, QI8_EINVAL, "null pointer");
+  const int L = log2_exact(rows);
+  QI8_REQUIRE(L >= 0 && L <= 15, QI8_ESHAPE, "Second-to-last dimension must be a power of 2 <= 32768, got %lld",
+              (long long)rows);
+  QI8_REQUIRE(cols > 0 && ld >= cols, QI8_ESHAPE, "bad sizes");
+  QI8_REQUIRE(final_mode >= FINAL_NONE && final_mode <= FINAL_DIV, QI8_EINVAL, "final mode %d", final_mode);
+  ColArgs ca{};
+  ca.w = nullptr; ca.M = rows; ca.N = cols; ca.M_pad = rows; ca.N_pad = cols; ca.x = x; ca.ld_x = ld;
+  ca.norm = factor;
+  return col_passes(true, ca, static_cast<cudaStream_t>(stream), final_mode);
+}
 
 int64_t qi8_quip_workspace_bytes(int64_t M, int64_t N) {
   if (M <= 0 || N <= 0) return 0;
@@ -307,6 +348,7 @@ int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, const flo
 
   ColArgs ca{};
   ca.w = w; ca.w_dtype = w_dtype; ca.M = M; ca.N = N; ca.M_pad = M_pad; ca.N_pad = N_pad; ca.x = X;
+  ca.ld_x = N_pad;
   ca.s_u = s_u; ca.s_v = s_v;
   ca.norm = (float)(1.0 / std::sqrt((double)M_pad));
   float* wd = dequant_out ? dequant_out : X;
@@ -323,19 +365,23 @@ int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, const flo
   if (rc) return rc;
   if (store_transformed) return QI8_OK;
 
-  ReqArgs qa{wd, ld_wd, M, N, q_out, scale_out, block, gword};
-  if (requant == QI8_REQ_BLOCK && N % block != 0) requant = QI8_REQ_ROW;
-  if (requant == QI8_REQ_ROW) {
-    requant_row_kernel<<<(unsigned)M, 256, 0, st>>>(qa);
-  } else if (requant == QI8_REQ_BLOCK) {
-    requant_block_kernel<<<(unsigned)M, 256, 0, st>>>(qa);
-  } else {
-    QI8_CUDA(cudaMemsetAsync(gword, 0, 4, st));
-    const int sms = sm_count() > 0 ? sm_count() : 148;
-    absmax_rows_kernel<<<sms * 4, 256, 0, st>>>(wd, ld_wd, M, N, gword);
-    requant_global_kernel<<<sms * 4, 256, 0, st>>>(qa);
-  }
-  return check_cuda(cudaGetLastError(), "requant launch");
+  return launch_requant(ReqArgs{wd, QI8_F32, ld_wd, M, N, q_out, scale_out, block, gword}, requant, st);
+}
+
+int qi8_requant_weight(const void* w, int w_dtype, int64_t M, int64_t N, int64_t ld_w, int requant, int block,
+                       int8_t* q_out, float* scale_out, void* workspace, int64_t workspace_bytes, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(w && q_out && scale_out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(M > 0 && N > 0 && ld_w >= N, QI8_ESHAPE, "bad sizes");
+  QI8_REQUIRE(w_dtype == QI8_BF16 || w_dtype == QI8_F16 || w_dtype == QI8_F32, QI8_EDTYPE, "weight dtype %d", w_dtype);
+  QI8_REQUIRE(requant == QI8_REQ_ROW || requant == QI8_REQ_GLOBAL || requant == QI8_REQ_BLOCK, QI8_EINVAL,
+              "requant scheme %d", requant);
+  if (requant == QI8_REQ_BLOCK)
+    QI8_REQUIRE(block == 32 || block == 64 || block == 128, QI8_ESHAPE, "block size %d not in {32, 64, 128}", block);
+  if (requant == QI8_REQ_GLOBAL)
+    QI8_REQUIRE(workspace && workspace_bytes >= 4, QI8_EINVAL, "global requant needs a 4-byte workspace");
+  return launch_requant(ReqArgs{w, w_dtype, ld_w, M, N, q_out, scale_out, block, static_cast<unsigned int*>(workspace)},
+                        requant, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -90,6 +90,19 @@ def fwht_rows(x: torch.Tensor, n_pad: Optional[int] = None, pre_sign: Optional[t
     return out.reshape(*x.shape[:-1], n_pad)
 
 
+def fwht_cols_(x: torch.Tensor, final_mode: int = 0, factor: float = 1.0) -> torch.Tensor:
+    """In-place FWHT down the columns of a contiguous fp32 matrix ``[rows, cols]``."""
+    L.require_cuda(x)
+    assert x.dtype == torch.float32 and x.dim() == 2 and x.stride(1) == 1, "x must be a row-major fp32 matrix"
+    rows, cols = x.shape
+    if rows & (rows - 1):
+        raise ValueError(f"Second-to-last dimension must be power of 2, got {rows}")
+    lib = L.load()
+    L.check(lib.qi8_fwht_cols(L.ptr(x), rows, cols, x.stride(0), final_mode, float(factor),
+                              L.stream_ptr(x.device)), "qi8_fwht_cols")
+    return x
+
+
 def unrotate_rows(y_had: torch.Tensor, sign_u: Optional[torch.Tensor], n_out: int,
                   bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """K3: ``(FWHT(y_had) * sign_u)[:, :n_out] + bias`` -> ``out_dtype``."""
@@ -221,6 +234,25 @@ def quip_convert(w: torch.Tensor, s_u: torch.Tensor, s_v: torch.Tensor, store_tr
                                  requant, block, L.ptr(q), L.ptr(s), L.ptr(deq), L.ptr(workspace), workspace.numel(),
                                  L.stream_ptr(w.device)), "qi8_quip_convert")
     return q, s, deq
+
+
+def requant_weight(w: torch.Tensor, requant: int = L.QI8_REQ_ROW, block: int = 128):
+    """QuIP requant rule without rotation (converters/quip_int8.py:1614-1669)."""
+    L.require_cuda(w)
+    assert w.dim() == 2 and w.stride(1) == 1, "weight must be a row-major 2-D tensor"
+    M, N = w.shape
+    q = torch.empty((M, N), dtype=torch.int8, device=w.device)
+    if requant == L.QI8_REQ_BLOCK and N % block == 0:
+        s = torch.empty((M, N // block, 1), dtype=torch.float32, device=w.device)
+    elif requant == L.QI8_REQ_GLOBAL:
+        s = torch.empty((), dtype=torch.float32, device=w.device)
+    else:
+        s = torch.empty((M, 1), dtype=torch.float32, device=w.device)
+    ws = torch.empty(64, dtype=torch.uint8, device=w.device)
+    lib = L.load()
+    L.check(lib.qi8_requant_weight(L.ptr(w), L.dtype_code(w.dtype), M, N, w.stride(0), requant, block, L.ptr(q),
+                                   L.ptr(s), L.ptr(ws), ws.numel(), L.stream_ptr(w.device)), "qi8_requant_weight")
+    return q, s
 
 
 def device_status(reset: bool = True) -> None:

@@ -109,6 +109,13 @@ QI8_API int qi8_fwht_rows(const void* x, int x_dtype, int64_t rows, int64_t n, i
                   int64_t n_pad, const float* pre_sign, const float* post_sign,
                   int normalize, float* out, void* stream);
 
+/* In-place FWHT down the columns of x [rows, cols] (row stride ld), rows a
+   power of two <= 32768: the row-dimension half of fast_hadamard_transform_2d
+   (utils/hadamard.py:467-516).  final_mode 0: un-normalized; 1: multiply by
+   factor; 2: divide by factor (the 2-D transform's x / sqrt(rows*cols)). */
+QI8_API int qi8_fwht_cols(float* x, int64_t rows, int64_t cols, int64_t ld, int final_mode, float factor,
+                          void* stream);
+
 /* K3: output un-rotation of a transformed-space linear:
      y = (FWHT_{n_pad}(y_had) / sqrt(n_pad) * sign_u)[:, :n_out] + bias
    (quip_int8_matmul steps 4-5, comfy/int8_kernels.py:1446-1450), written as
@@ -174,6 +181,15 @@ QI8_API int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, c
                      const float* s_v, int store_transformed, int requant, int block,
                      int8_t* q_out, float* scale_out, float* dequant_out, void* workspace,
                      int64_t workspace_bytes, void* stream);
+
+/* Original-space requantization of a weight W[M,N] (row stride ld_w) with the
+   QuIP requant rule (converters/quip_int8.py:1614-1669): scale =
+   max(amax/127, 1e-12), q = rint(w / scale) in [-127, 127]; QI8_REQ_ROW ->
+   scale [M], QI8_REQ_GLOBAL -> scale [1] (workspace >= 4 bytes),
+   QI8_REQ_BLOCK -> scale [M, N/block] (per-row fallback if N % block != 0). */
+QI8_API int qi8_requant_weight(const void* w, int w_dtype, int64_t M, int64_t N, int64_t ld_w, int requant,
+                               int block, int8_t* q_out, float* scale_out, void* workspace,
+                               int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

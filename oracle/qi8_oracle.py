@@ -283,9 +283,13 @@ def int8_gemm_block(a: np.ndarray, a_s: np.ndarray, b: np.ndarray, b_s: np.ndarr
 
 def gelu_f32(x: np.ndarray) -> np.ndarray:
     """Exact-erf GELU ``0.5 x (1 + erf(x / sqrt 2))`` (torch ``F.gelu`` default)."""
-    from math import erf
     xf = np.asarray(x, dtype=np.float64)
-    v = np.vectorize(erf)(xf / math.sqrt(2.0))
+    try:
+        from scipy.special import erf as _erf
+        v = _erf(xf / math.sqrt(2.0))
+    except ImportError:  # pragma: no cover
+        from math import erf
+        v = np.vectorize(erf)(xf / math.sqrt(2.0))
     return (0.5 * xf * (1.0 + v)).astype(np.float32)
 
 
