@@ -2,7 +2,7 @@
 
 Workload (one step): the DiT MLP pair with block-128 K scales --
 x [4096, 3072] bf16 -> per-token int8 (K1) -> W1 [12288, 3072] int8 GEMM with
-per-128-K-block promotion + GELU epilogue (K2) -> per-token int8 (K1) ->
+per-128-K-block promotion (K2) -> GELU + per-token int8 (K1) ->
 W2 [3072, 12288] int8 GEMM (K2) -> bf16 [4096, 3072].
 Metric: W8A8 linear TOPS (2 * M * N * K per GEMM, both GEMMs), whole job.
 
@@ -224,8 +224,8 @@ def main():
     lib = L.load()
     sp = L.stream_ptr(device)
 
-    def k1(src, n, dst_q, dst_s):
-        L.check(lib.qi8_quant_rows(L.ptr(src), L.QI8_BF16, T, n, n, L.QI8_Q_TOKEN, 128, L.ptr(dst_q), n,
+    def k1(src, n, dst_q, dst_s, mode=L.QI8_Q_TOKEN):
+        L.check(lib.qi8_quant_rows(L.ptr(src), L.QI8_BF16, T, n, n, mode, 128, L.ptr(dst_q), n,
                                    L.ptr(dst_s), sp))
 
     xs = torch.empty((T, 1), dtype=torch.float32, device=device)
@@ -242,10 +242,10 @@ def main():
         k1(x, H, xq, xs)
         if ev:
             ev[0].record(stream)
-        gemm(xq, xs, q1, s1, h, L.QI8_ACT_GELU)
+        gemm(xq, xs, q1, s1, h, L.QI8_ACT_NONE)
         if ev:
             ev[1].record(stream)
-        k1(h, F_, hq, hs)
+        k1(h, F_, hq, hs, L.QI8_Q_TOKEN | L.QI8_Q_GELU)  # GELU fused into the per-token quantization
         if ev:
             ev[2].record(stream)
         gemm(hq, hs, q2, s2, y, L.QI8_ACT_NONE)

@@ -29,7 +29,7 @@ QI8_EUNSUPPORTED = -7
 # element types
 QI8_BF16, QI8_F16, QI8_F32, QI8_I8, QI8_I32 = 0, 1, 2, 3, 4
 # row quantization modes
-QI8_Q_TOKEN, QI8_Q_BLOCK = 0, 1
+QI8_Q_TOKEN, QI8_Q_BLOCK, QI8_Q_GELU = 0, 1, 0x100
 # scale kinds
 QI8_S_NONE, QI8_S_SCALAR, QI8_S_ROW, QI8_S_ROW_KBLOCK, QI8_S_TILE128 = 0, 1, 2, 3, 4
 # epilogue activation

@@ -43,11 +43,20 @@ constexpr int B_BYTES = BN * BK;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
-constexpr int THREADS = 32 * 10;
+constexpr int THREADS = 32 * 12;  // three warpgroups; warps 10 and 11 only donate registers
+// Register split of the block-scaled kernel: launched at 168 registers per
+// thread (384 x 168 = 64512 <= 65536; three warps per SM sub-partition), the
+// control warpgroup drops to 56 and the two epilogue warpgroups rise to 224:
+// 256 x 224 + 128 x 56 == 384 x 168.  The host refuses to launch if the
+// compiled kernel does not use exactly LAUNCH_REGS registers.
+constexpr int LAUNCH_REGS = 168;
+constexpr int EPI_REGS = 240;
+constexpr int CTRL_REGS = 24;
+static_assert(256 * EPI_REGS + 128 * CTRL_REGS == THREADS * LAUNCH_REGS, "register split must balance");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SCALE_BYTES = NUM_EPI_WARPS * 128 * 4;
+constexpr int STAGE_SCRATCH_BYTES = 3 * NUM_EPI_WARPS * 128 * 4;  // column scales, bias, per-kb scales
 constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + SCALE_BYTES + NUM_BARS * 8 + 16;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES + NUM_BARS * 8 + 16;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;  // 0.2 s when cleaning up
 
@@ -64,7 +73,7 @@ constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >
 
 struct GemmArgs {
   int M, N, K, KB;
-  int m_tiles, n_tiles, num_tiles;
+  int r_tiles, c_tiles, num_tiles;  // tiles over the TMEM-lane operand (128 rows) and the column operand (256 rows)
   const float* a_scale;
   int a_kind;
   const float* b_scale;
@@ -109,7 +118,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 // Bounded wait: true when the phase completed; false on expiry or when
 // another role of this CTA already gave up.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                        unsigned int* status, unsigned int bit, uint64_t limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -184,6 +193,21 @@ __device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v) {
       "r"(v)
       : "memory");
 }
+// Shared-memory float2 load that stays in program order with the tcgen05
+// asm statements around it (keeps scale registers from being hoisted).
+__device__ __forceinline__ float2 lds_f2(const float* p) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
@@ -198,14 +222,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // ------------------------------------------------------------ epilogue
-__device__ __forceinline__ float finish_value(float y, int n, const GemmArgs& p) {
-  if (p.bias) y = __fadd_rn(y, load_as_f32(p.bias, p.bias_dtype, n));
-  if (p.act == QI8_ACT_GELU) {
-    if (p.out_dtype == QI8_BF16) y = __bfloat162float(__float2bfloat16_rn(y));
-    else if (p.out_dtype == QI8_F16) y = __half2float(__float2half_rn(y));
-    y = gelu_erf(y);
-  }
-  return y;
+// GELU of the linear output as the reference computes it on a bf16/fp16
+// tensor: the value is first rounded to the output dtype.
+__device__ __forceinline__ float act_gelu(float y, int out_dtype) {
+  if (out_dtype == QI8_BF16) y = __bfloat162float(__float2bfloat16_rn(y));
+  else if (out_dtype == QI8_F16) y = __half2float(__float2half_rn(y));
+  return gelu_erf(y);
 }
 
 // Stores 32 consecutive fp32 results of row m starting at column n0.
@@ -319,7 +341,11 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
   return 1.0f;
 }
 
-template <bool PROMOTE>
+// SWAP: the weight tile is the MMA A operand (TMEM lanes = output features)
+// and the activation tile the B operand (TMEM columns = tokens).  Used when
+// the weight scale varies per (row, K block) and the activation scale does
+// not, so that every epilogue thread promotes with one scalar per K block.
+template <bool PROMOTE, bool SWAP>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs p) {
@@ -329,8 +355,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sb = smem_raw + (base - raw);
   const uint32_t sA = base;
   const uint32_t sB = base + STAGES * A_BYTES;
-  float* sscale = reinterpret_cast<float*>(sb + STAGES * (A_BYTES + B_BYTES));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES * (A_BYTES + B_BYTES) + SCALE_BYTES);
+  float* scol = reinterpret_cast<float*>(sb + STAGES * (A_BYTES + B_BYTES));  // [8 warps][128] column scales
+  float* sbias = scol + NUM_EPI_WARPS * 128;                                   // [8 warps][128] bias
+  float* skb = sbias + NUM_EPI_WARPS * 128;                                    // [8 warps][128] per-kb scales
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
@@ -384,6 +412,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
   }
 
+  if (warp >= NUM_EPI_WARPS) {
+    // control warpgroup: producer, MMA issuer and two idle warps.  In the
+    // block-scaled kernel it hands registers to the epilogue warpgroups.
+    if constexpr (PROMOTE) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CTRL_REGS));
   if (warp == PRODUCER_WARP) {
     if (lane == 0) {
       int s = 0;
@@ -391,8 +423,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued = 0, issued_ph = 0;  // per-stage: load in flight, and its phase
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const int m0 = (tile % p.m_tiles) * BM;
-        const int n0 = (tile / p.m_tiles) * BN;
+        const int m0 = (tile % p.r_tiles) * BM;
+        const int n0 = (tile / p.r_tiles) * BN;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.status, ST_GEMM_PRODUCER, WAIT_LIMIT_NS)) {
             ok = false;
@@ -458,121 +490,208 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) mbar_wait(drain_bar, 0, abort_flag, p.status, ST_GEMM_DRAIN, WAIT_LIMIT_NS);
       else drain_wait(drain_bar, 0);
     }
+  }
   } else {
     // ------------------------------------------------------- epilogue
+    if constexpr (PROMOTE) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(EPI_REGS));
     const int quad = warp & 3, half = warp >> 2;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    float* my_sc = sscale + warp * 128;
+    float* my_col = scol + warp * 128;
+    float* my_bias = sbias + warp * 128;
+    float* my_kb = skb + warp * 128;
+    const int R = SWAP ? p.N : p.M;  // rows on TMEM lanes
+    const int C = SWAP ? p.M : p.N;  // rows on TMEM columns
     int au = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-      const int m = (tile % p.m_tiles) * BM + quad * 32 + lane;
-      const int ncol0 = (tile / p.m_tiles) * BN + half * 128;
-      const bool row_ok = m < p.M;
-      const bool cols_ok = ncol0 < p.N;
+      const int rr = (tile % p.r_tiles) * BM + quad * 32 + lane;  // this thread's row (m, or n when SWAP)
+      const int cc0 = (tile / p.r_tiles) * BN + half * 128;       // first column of this warp
+      const bool row_ok = rr < R;
+      const bool cols_ok = cc0 < C;
+      // per-column factors of this warp's 128 columns (coalesced, once per tile):
+      // weight scale and bias per output feature, or (SWAP) activation scale per token
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int cc = cc0 + c * 32 + lane;
+        if constexpr (SWAP) {
+          my_col[c * 32 + lane] = cc < C ? row_scale(p.a_scale, p.a_kind, cc) : 0.0f;
+        } else {
+          my_col[c * 32 + lane] = cc < C ? row_scale(p.b_scale, p.b_kind, cc) : 0.0f;
+          my_bias[c * 32 + lane] = (p.bias && cc < C) ? load_as_f32(p.bias, p.bias_dtype, cc) : 0.0f;
+        }
+      }
+      __syncwarp();
+      // this thread's final row factor (and bias when the row is an output feature)
+      float frow = 1.0f, brow = 0.0f;
+      if (row_ok) {
+        if constexpr (SWAP) {
+          frow = row_scale(p.b_scale, p.b_kind, rr);
+          if (p.bias) brow = load_as_f32(p.bias, p.bias_dtype, rr);
+        } else {
+          frow = row_scale(p.a_scale, p.a_kind, rr);
+        }
+      }
       if constexpr (PROMOTE) {
         float2 acc[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) acc[i] = make_float2(0.0f, 0.0f);
-        const bool a_kb = p.a_kind == QI8_S_ROW_KBLOCK;
-        const bool b_col = p.b_kind == QI8_S_ROW_KBLOCK;
+        // K-block scale: one scalar per thread, except a per-column weight
+        // scale combined with per-(row, K block) activation scales
+        const bool a_kb = !SWAP && p.a_kind == QI8_S_ROW_KBLOCK;
+        const bool b_col = !SWAP && p.b_kind == QI8_S_ROW_KBLOCK;
         const bool b_tile = p.b_kind == QI8_S_TILE128;
         for (int kb = 0; kb < KB; ++kb, ++au) {
           const int buf = au & 1;
-          float sa = 1.0f;
-          if (a_kb) sa = row_ok ? __ldg(p.a_scale + (int64_t)m * KB + kb) : 0.0f;
-          float sconst = sa;
-          if (b_tile) sconst = __fmul_rn(sa, cols_ok ? __ldg(p.b_scale + (int64_t)(ncol0 >> 7) * KB + kb) : 0.0f);
-          if (b_col) {
-            __syncwarp();
+          float sk = 1.0f;
+          if constexpr (SWAP) {
+            sk = row_ok ? __ldg(p.b_scale + (int64_t)rr * KB + kb) : 0.0f;
+          } else {
+            if (a_kb) sk = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
+            if (b_tile) sk = __fmul_rn(sk, cols_ok ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f);
+            if (b_col) {
+              __syncwarp();
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int n = ncol0 + c * 32 + lane;
-              my_sc[c * 32 + lane] = n < p.N ? __ldg(p.b_scale + (int64_t)n * KB + kb) : 0.0f;
+              for (int c = 0; c < 4; ++c) {
+                const int n = cc0 + c * 32 + lane;
+                my_kb[c * 32 + lane] = n < p.N ? __ldg(p.b_scale + (int64_t)n * KB + kb) : 0.0f;
+              }
+              __syncwarp();
             }
-            __syncwarp();
           }
+          const float2 sk2 = make_float2(sk, sk);
           if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const bool last = kb == KB - 1;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t r[16];
-            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + c * 16);
-            tmem_ld16(ta, r);
+          for (int rnd = 0; rnd < 2; ++rnd) {
+            uint32_t r[4][16];
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + rnd * 64);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld16(ta + c * 16, r[c]);
             tmem_wait_ld();
-            tmem_fill16(ta, MAGIC_BITS);  // re-bias for this buffer's next K block
+            if (!last) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float2 f = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
-              float2 sc;
-              if (b_col) {
-                sc = *reinterpret_cast<const float2*>(my_sc + c * 16 + 2 * j);
-                if (a_kb) sc = __fmul2_rn(sc, make_float2(sa, sa));
-              } else {
-                sc = make_float2(sconst, sconst);
-              }
-              acc[c * 8 + j] = __ffma2_rn(f, sc, acc[c * 8 + j]);
+              for (int c = 0; c < 4; ++c) tmem_fill16(ta + c * 16, MAGIC_BITS);  // re-bias for the next K block
             }
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(tempty_bar(buf));
-        }
-        if (!ok) break;
-        if (row_ok && cols_ok) {
-          const float fa = row_scale(p.a_scale, p.a_kind, m);
 #pragma unroll
-          for (int g = 0; g < 16; ++g) {
-            const int n0 = ncol0 + g * 8;
-            if (n0 < p.N) {
-              float y[8];
+            for (int c = 0; c < 4; ++c) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int n = n0 + j < p.N ? n0 + j : p.N - 1;
-                const float v = (j & 1) ? acc[g * 4 + (j >> 1)].y : acc[g * 4 + (j >> 1)].x;
-                y[j] = finish_value(__fmul_rn(__fmul_rn(v, fa), row_scale(p.b_scale, p.b_kind, n)), n, p);
+                const int col = rnd * 64 + c * 16 + 2 * j;
+                float2 f = make_float2(__uint_as_float(r[c][2 * j]), __uint_as_float(r[c][2 * j + 1]));
+                f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
+                float2 sc = sk2;
+                if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
+                acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
               }
-              store_row8(p, m, n0, y);
             }
           }
+          if (!last) {
+            // the last K block's buffer stays held for the tile epilogue below
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(buf));
+          }
         }
+        if (!ok) break;
+        // ---- tile epilogue: final scales in registers, staged through the
+        // held TMEM buffer so the store loop below stays compact
+        const int bufl = (au - 1) & 1;
+        const uint32_t tl = tmem_base + lane_base + (uint32_t)(bufl * BN + half * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = c * 16 + j;
+            const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
+            float y;
+            if constexpr (SWAP) y = __fadd_rn(__fmul_rn(__fmul_rn(a, my_col[col]), frow), brow);
+            else y = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), my_col[col]), my_bias[col]);
+            v[j] = __float_as_uint(y);
+          }
+          tmem_st16(tl + c * 16, v);
+        }
+        tmem_wait_st();
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+          tmem_ld16(tl + c * 16, v);
+          tmem_wait_ld();
+          tmem_fill16(tl + c * 16, MAGIC_BITS);  // re-bias for the next tile
+          const int col0 = cc0 + c * 16;
+          if (!row_ok || col0 >= C) continue;
+          float y[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            y[j] = __uint_as_float(v[j]);
+            if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
+          }
+          if constexpr (SWAP) {
+            // thread = output feature rr; the 16 values are 16 consecutive tokens
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (col0 + j < C) {
+                const int64_t o = (int64_t)(col0 + j) * p.ld_out + rr;
+                if (p.out_dtype == QI8_BF16) static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(y[j]);
+                else if (p.out_dtype == QI8_F16) static_cast<__half*>(p.out)[o] = __float2half_rn(y[j]);
+                else static_cast<float*>(p.out)[o] = y[j];
+              }
+            }
+          } else {
+            store_row8(p, rr, col0, *reinterpret_cast<const float(*)[8]>(&y[0]));
+            if (col0 + 8 < C) store_row8(p, rr, col0 + 8, *reinterpret_cast<const float(*)[8]>(&y[8]));
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(bufl));
       } else {
+        const int m = rr;
+        const int ncol0 = cc0;
+        const float fa = frow;
         const int buf = au & 1;
         if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float xs = row_ok ? row_scale(p.a_scale, p.a_kind, m) : 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + c * 32), r);
+#pragma unroll
+        for (int rnd = 0; rnd < 2; ++rnd) {
+          uint32_t r[2][32];
+          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + rnd * 64);
+          tmem_ld32(ta, r[0]);
+          tmem_ld32(ta + 32, r[1]);
           tmem_wait_ld();
-          if (c == 3) {
+          if (rnd == 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(buf));
           }
-          const int n0 = ncol0 + c * 32;
-          if (!row_ok || n0 >= p.N) continue;
-          if (p.out_dtype == QI8_I32) {
-            store_row32_i32(p, m, n0, r);
-          } else {
-            float y[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j < p.N ? n0 + j : p.N - 1;
-              // optimized_linear: res.float() * (x_s * w_s) + bias  (comfy/quant_ops.py:472-473)
-              const float s = __fmul_rn(xs, row_scale(p.b_scale, p.b_kind, n));
-              y[j] = finish_value(__fmul_rn(__int2float_rn((int)r[j]), s), n, p);
+          for (int c = 0; c < 2; ++c) {
+            const int cc = rnd * 64 + c * 32;  // column within this warp's 128
+            const int n0 = ncol0 + cc;
+            if (!row_ok || n0 >= p.N) continue;
+            if (p.out_dtype == QI8_I32) {
+              store_row32_i32(p, m, n0, r[c]);
+            } else {
+              float y[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                // optimized_linear: res.float() * (x_s * w_s) + bias  (comfy/quant_ops.py:472-473)
+                y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(fa, my_col[cc + j]));
+                if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
+                if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
+              }
+              store_row32(p, m, n0, y);
             }
-            store_row32(p, m, n0, y);
           }
         }
         ++au;
@@ -620,7 +739,7 @@ int make_map(CUtensorMap* map, const int8_t* ptr, int64_t rows, int64_t K, uint3
   return QI8_OK;
 }
 
-bool g_attr_set[2][64];
+bool g_attr_set[3][64];
 
 }  // namespace
 }  // namespace qi8
@@ -656,17 +775,22 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   QI8_REQUIRE(act == QI8_ACT_NONE || act == QI8_ACT_GELU, QI8_EINVAL, "act %d", act);
   if (M == 0) return QI8_OK;
 
+  // weights on TMEM lanes when their scale varies per (row, K block) and the activations' does not
+  const bool swap = promote && b_kind == QI8_S_ROW_KBLOCK && a_kind != QI8_S_ROW_KBLOCK;
+  const int8_t* Rop = swap ? B : A;
+  const int8_t* Cop = swap ? A : B;
+  const int64_t Rrows = swap ? N : M, Crows = swap ? M : N;
   CUtensorMap mapA, mapB;
-  int rc = make_map(&mapA, A, M, K, BM);
+  int rc = make_map(&mapA, Rop, Rrows, K, BM);
   if (rc) return rc;
-  rc = make_map(&mapB, B, N, K, BN);
+  rc = make_map(&mapB, Cop, Crows, K, BN);
   if (rc) return rc;
 
   GemmArgs p{};
   p.M = (int)M; p.N = (int)N; p.K = (int)K; p.KB = (int)((K + BK - 1) / BK);
-  p.m_tiles = (int)((M + BM - 1) / BM);
-  p.n_tiles = (int)((N + BN - 1) / BN);
-  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.r_tiles = (int)((Rrows + BM - 1) / BM);
+  p.c_tiles = (int)((Crows + BN - 1) / BN);
+  p.num_tiles = p.r_tiles * p.c_tiles;
   p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
   p.bias = bias; p.bias_dtype = bias_dtype; p.out = out; p.out_dtype = out_dtype; p.ld_out = ld_out;
   p.act = act;
@@ -674,10 +798,19 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
 
   int dev = 0;
   QI8_CUDA(cudaGetDevice(&dev));
-  auto kern = promote ? gemm_i8_kernel<true> : gemm_i8_kernel<false>;
-  if (dev < 64 && !g_attr_set[promote][dev]) {
+  auto kern = !promote ? gemm_i8_kernel<false, false> : (swap ? gemm_i8_kernel<true, true> : gemm_i8_kernel<true, false>);
+  const int variant = !promote ? 0 : (swap ? 2 : 1);
+  if (dev < 64 && !g_attr_set[variant][dev]) {
     QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    g_attr_set[promote][dev] = true;
+    if (promote) {
+      // the in-kernel register split assumes exactly LAUNCH_REGS registers per thread at launch
+      cudaFuncAttributes fa{};
+      QI8_CUDA(cudaFuncGetAttributes(&fa, kern));
+      QI8_REQUIRE(fa.numRegs == LAUNCH_REGS, QI8_EUNSUPPORTED,
+                  "block-scaled GEMM compiled with %d registers per thread, register split needs %d", fa.numRegs,
+                  LAUNCH_REGS);
+    }
+    g_attr_set[variant][dev] = true;
   }
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = p.num_tiles < sms ? p.num_tiles : sms;

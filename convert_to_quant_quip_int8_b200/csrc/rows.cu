@@ -77,7 +77,16 @@ struct QArgs {
 
 constexpr int QR_THREADS = 256;
 
-template <typename T, int CPT, int MODE>
+// Exact-erf GELU of an element as torch computes it on a T tensor: fp32 math,
+// result rounded to T.
+template <typename T>
+__device__ __forceinline__ float gelu_in_dtype(float v) {
+  const float g = gelu_erf(v);
+  if constexpr (sizeof(T) == 2) return to_f32<T>(Elem<T>::from_f32(g));
+  return g;
+}
+
+template <typename T, int CPT, int MODE, bool GELU>
 __global__ void __launch_bounds__(QR_THREADS) quant_rows_kernel(QArgs a) {
   __shared__ float red[32];
   const int t = threadIdx.x;
@@ -92,6 +101,10 @@ __global__ void __launch_bounds__(QR_THREADS) quant_rows_kernel(QArgs a) {
     int c = r * QR_THREADS + t;
     if (c < nc) {
       load_run<T, 8>(xr, c * 8, a.n, a.vec != 0, v[r]);
+      if constexpr (GELU) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[r][e] = gelu_in_dtype<T>(v[r][e]);
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[r][e] = 0.0f;
@@ -145,19 +158,24 @@ __global__ void __launch_bounds__(QR_THREADS) quant_rows_kernel(QArgs a) {
 
 // Scalar fallback for rows whose width is not a multiple of 8 (TOKEN) or
 // whose pointers are not vector aligned; reads the row twice.
-template <typename T>
+template <typename T, bool GELU>
 __global__ void __launch_bounds__(QR_THREADS) quant_rows_scalar_kernel(QArgs a) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
   int8_t* qr = a.q + row * a.ld_q;
+  auto val = [&](int c) {
+    const float v = to_f32<T>(xr[c]);
+    if constexpr (GELU) return gelu_in_dtype<T>(v);
+    return v;
+  };
   float local = 0.0f;
-  for (int c = threadIdx.x; c < a.n; c += blockDim.x) local = fmaxf(local, fabsf(to_f32<T>(xr[c])));
+  for (int c = threadIdx.x; c < a.n; c += blockDim.x) local = fmaxf(local, fabsf(val(c)));
   const float amax = block_max(local, red);
   const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
   const float rcp = __frcp_rn(s);
   for (int c = threadIdx.x; c < a.n; c += blockDim.x)
-    qr[c] = rint_clamp(__fmul_rn(to_f32<T>(xr[c]), rcp), -128.0f, 127.0f);
+    qr[c] = rint_clamp(__fmul_rn(val(c), rcp), -128.0f, 127.0f);
   if (threadIdx.x == 0) a.scale[row] = s;
 }
 
@@ -386,17 +404,17 @@ __global__ void __launch_bounds__(256) quant_tile128_kernel(const T* __restrict_
   if (threadIdx.x == 0) scale[tr * nbc + tc] = s;
 }
 
-template <typename T, int MODE>
+template <typename T, int MODE, bool GELU>
 int launch_quant_rows_T(const QArgs& a, int64_t rows, cudaStream_t st) {
   const int nc = (a.n + 7) / 8;
   const int cpt = (nc + QR_THREADS - 1) / QR_THREADS;
   if (a.n % 8 != 0 || !a.vec) {
     if (MODE != QI8_Q_TOKEN) return fail(QI8_EALIGN, "block quantization needs 16-byte aligned rows");
-    quant_rows_scalar_kernel<T><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
+    quant_rows_scalar_kernel<T, GELU><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
     return check_cuda(cudaGetLastError(), "quant_rows_scalar_kernel launch");
   }
   switch (cpt) {
-#define QI8_CPT(c) case c: quant_rows_kernel<T, c, MODE><<<(unsigned)rows, QR_THREADS, 0, st>>>(a); break;
+#define QI8_CPT(c) case c: quant_rows_kernel<T, c, MODE, GELU><<<(unsigned)rows, QR_THREADS, 0, st>>>(a); break;
     QI8_CPT(1) QI8_CPT(2)
     case 3: QI8_CPT(4)
     case 5: case 6: case 7: QI8_CPT(8)
@@ -404,17 +422,17 @@ int launch_quant_rows_T(const QArgs& a, int64_t rows, cudaStream_t st) {
 #undef QI8_CPT
     default:
       if (MODE != QI8_Q_TOKEN) return fail(QI8_ESHAPE, "row width %d > 32768", a.n);
-      quant_rows_scalar_kernel<T><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
+      quant_rows_scalar_kernel<T, GELU><<<(unsigned)rows, QR_THREADS, 0, st>>>(a);
   }
   return check_cuda(cudaGetLastError(), "quant_rows_kernel launch");
 }
 
-template <int MODE>
+template <int MODE, bool GELU>
 int launch_quant_rows(int dtype, const QArgs& a, int64_t rows, cudaStream_t st) {
   switch (dtype) {
-    case QI8_BF16: return launch_quant_rows_T<__nv_bfloat16, MODE>(a, rows, st);
-    case QI8_F16: return launch_quant_rows_T<__half, MODE>(a, rows, st);
-    case QI8_F32: return launch_quant_rows_T<float, MODE>(a, rows, st);
+    case QI8_BF16: return launch_quant_rows_T<__nv_bfloat16, MODE, GELU>(a, rows, st);
+    case QI8_F16: return launch_quant_rows_T<__half, MODE, GELU>(a, rows, st);
+    case QI8_F32: return launch_quant_rows_T<float, MODE, GELU>(a, rows, st);
     default: return fail(QI8_EDTYPE, "input dtype %d not in {bf16, f16, f32}", dtype);
   }
 }
@@ -446,11 +464,16 @@ int qi8_quant_rows(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t 
   QArgs a{x, ld_x, (int)n, q_out, ld_q, scale_out, 0};
   a.vec = aligned16(x) && (ld_x * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(q_out) & 7) == 0 && ld_q % 8 == 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (mode == QI8_Q_TOKEN) return launch_quant_rows<QI8_Q_TOKEN>(x_dtype, a, rows, st);
+  const bool gelu = (mode & QI8_Q_GELU) != 0;
+  mode &= ~QI8_Q_GELU;
+  if (mode == QI8_Q_TOKEN)
+    return gelu ? launch_quant_rows<QI8_Q_TOKEN, true>(x_dtype, a, rows, st)
+                : launch_quant_rows<QI8_Q_TOKEN, false>(x_dtype, a, rows, st);
   if (mode == QI8_Q_BLOCK) {
     QI8_REQUIRE(block == 128, QI8_ESHAPE, "block size must be 128 (got %d)", block);
     QI8_REQUIRE(n % 128 == 0, QI8_ESHAPE, "Last dimension size must be divisible by block_size (block_size=128)");
-    return launch_quant_rows<QI8_Q_BLOCK>(x_dtype, a, rows, st);
+    return gelu ? launch_quant_rows<QI8_Q_BLOCK, true>(x_dtype, a, rows, st)
+                : launch_quant_rows<QI8_Q_BLOCK, false>(x_dtype, a, rows, st);
   }
   return fail(QI8_EINVAL, "unknown quantization mode %d", mode);
 }

@@ -40,13 +40,14 @@ def quant_rows(x: torch.Tensor, mode: int = L.QI8_Q_TOKEN, block: int = 128) -> 
     x2 = _rows2d(x)
     rows, n = x2.shape
     q = torch.empty((rows, n), dtype=torch.int8, device=x.device)
-    ns = 1 if mode == L.QI8_Q_TOKEN else n // block
+    base_mode = mode & 0xFF
+    ns = 1 if base_mode == L.QI8_Q_TOKEN else n // block
     s = torch.empty((rows, ns), dtype=torch.float32, device=x.device)
     lib = L.load()
     L.check(lib.qi8_quant_rows(L.ptr(x2), L.dtype_code(x2.dtype), rows, n, x2.stride(0), mode, block,
                                L.ptr(q), n, L.ptr(s), L.stream_ptr(x.device)), "qi8_quant_rows")
     q = q.reshape(x.shape)
-    if mode == L.QI8_Q_TOKEN:
+    if base_mode == L.QI8_Q_TOKEN:
         return q, s.reshape(*x.shape[:-1], 1)
     return q, s.reshape(*x.shape[:-1], ns)
 

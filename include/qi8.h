@@ -54,7 +54,11 @@ enum {
   QI8_Q_TOKEN = 0,
   /* per (row, 128-block): s = amax/127; q = trunc(x / s)
      -- Triton act_quant, comfy/int8_kernels.py:72-123 */
-  QI8_Q_BLOCK = 1
+  QI8_Q_BLOCK = 1,
+  /* flag for qi8_quant_rows: apply exact-erf GELU to every element first
+     (rounded to the input dtype, as torch's gelu on that tensor), then
+     quantize -- the GELU between the two projections of a DiT MLP */
+  QI8_Q_GELU = 0x100
 };
 
 /* GEMM scale kinds */

@@ -110,6 +110,19 @@ def test_quant_rows_token_random(n, dtype):
     assert np.array_equal(np_(q), qr) and np.array_equal(np_(s), sr)
 
 
+@pytest.mark.parametrize("n", [3072, 12288, 1000])
+def test_quant_rows_gelu_fused(n):
+    # GELU between the DiT MLP projections: torch gelu on the bf16 tensor, then per-token quant
+    r = rng(n + 1)
+    h = torch.from_numpy((r.standard_normal((9, n)) * 2).astype(np.float32)).to(torch.bfloat16)
+    q, s = ops.quant_rows(h.to(dev()), L.QI8_Q_TOKEN | L.QI8_Q_GELU)
+    g = torch.nn.functional.gelu(h.float()).to(torch.bfloat16).float().numpy()
+    qr, sr = O.quantize_int8_axiswise(g)
+    # erff (CUDA) vs erf (CPU) may differ in the last ulp before the bf16 rounding
+    assert np.mean(np_(q) != qr) < 1e-3 and np.max(np.abs(np_(q).astype(int) - qr)) <= 1
+    assert np.allclose(np_(s), sr, rtol=1e-2)
+
+
 def test_quant_rows_block_golden(golden):
     g = golden("triton_quant.npz")
     q, s = ops.quant_rows(bf16_cu(g["x_bf16"]), mode=L.QI8_Q_BLOCK)
