@@ -60,6 +60,7 @@ SIGNATURES = {
     "qi8_quant_weight": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _P, _I64, _P]),
     "qi8_quip_workspace_bytes": (_I64, [_I64, _I64]),
     "qi8_quip_convert": (_I, [_P, _I, _I64, _I64, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I64, _P]),
+    "qi8_quip_convert_noalloc": (_I, [_P, _I, _I64, _I64, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qi8_requant_weight": (_I, [_P, _I, _I64, _I64, _I64, _I, _I, _P, _P, _P, _I64, _P]),
 }
 

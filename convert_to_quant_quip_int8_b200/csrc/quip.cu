@@ -298,6 +298,32 @@ int col_passes(bool forward, const ColArgs& base, cudaStream_t st, int final = F
   return QI8_OK;
 }
 
+// ------------------------------------------- converter without allocation
+// Scratch of qi8_quip_convert_noalloc: one fp32 plane of at most
+// NOALLOC_MAX_ELEMS = 2^24 padded elements (a 4096 x 4096 weight) plus the
+// 256-byte tail the global requant uses -- 64 MiB + 256 B that every device
+// which loads this library keeps until the process exits.
+constexpr int64_t NOALLOC_MAX_ELEMS = int64_t(1) << 24;
+constexpr int64_t NOALLOC_BYTES = NOALLOC_MAX_ELEMS * 4 + 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (host code only sees a stand-in for the symbol).
+void* g_noalloc_ptr[64];
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  QI8_CUDA(cudaGetDevice(&dev));
+  QI8_REQUIRE(dev >= 0 && dev < 64, QI8_EUNSUPPORTED, "device ordinal %d out of range", dev);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    QI8_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return QI8_OK;
+}
+
 }  // namespace
 }  // namespace qi8
 
@@ -366,6 +392,26 @@ int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, const flo
   if (store_transformed) return QI8_OK;
 
   return launch_requant(ReqArgs{wd, QI8_F32, ld_wd, M, N, q_out, scale_out, block, gword}, requant, st);
+}
+
+int qi8_quip_convert_noalloc(const void* w, int w_dtype, int64_t M, int64_t N, const float* s_u, const float* s_v,
+                             int store_transformed, int requant, int block, int8_t* q_out, float* scale_out,
+                             float* dequant_out, void* stream) {
+  QI8_REQUIRE(M > 0 && N > 0, QI8_ESHAPE, "bad sizes M=%lld N=%lld", (long long)M, (long long)N);
+  const int64_t padded = next_pow2(M) * next_pow2(N);
+  QI8_REQUIRE(padded <= NOALLOC_MAX_ELEMS, QI8_ESHAPE,
+              "qi8_quip_convert_noalloc: padded weight %lld x %lld = %lld elements exceeds the built-in scratch of "
+              "%lld elements (64 MiB); use qi8_quip_convert with a caller workspace",
+              (long long)next_pow2(M), (long long)next_pow2(N), (long long)padded, (long long)NOALLOC_MAX_ELEMS);
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Every cell of the fp32 plane the call reads is written earlier in the
+  // same call, and the 4-byte global-amax word is zeroed before use, so the
+  // previous call's contents never leak into this one.
+  return qi8_quip_convert(w, w_dtype, M, N, s_u, s_v, store_transformed, requant, block, q_out, scale_out,
+                          dequant_out, scratch, NOALLOC_BYTES, stream);
 }
 
 int qi8_requant_weight(const void* w, int w_dtype, int64_t M, int64_t N, int64_t ld_w, int requant, int block,

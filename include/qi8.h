@@ -186,6 +186,24 @@ QI8_API int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, c
                      int8_t* q_out, float* scale_out, float* dequant_out, void* workspace,
                      int64_t workspace_bytes, void* stream);
 
+/* qi8_quip_convert without a caller workspace (no counterpart in the
+   reference).  For callers that cannot allocate device memory: a host
+   program binding this C ABI from a runtime that has no CUDA allocator of
+   its own, or a process whose device memory is already reserved by another
+   allocator (PyTorch's caching allocator holds freed blocks, so a fresh
+   cudaMalloc can fail although memory is free inside its pool).  The scratch
+   is a fixed 64 MiB + 256 B array inside the library, held by every device
+   that loads it until exit; M_pad * N_pad must be <= 2^24 (e.g. 4096 x 4096),
+   larger weights are rejected with QI8_ESHAPE.  Nothing is allocated or freed.
+   The first call on a device looks up the array's device address (issue it
+   before any stream capture).  All calls share the one array: calls that
+   overlap on the GPU (different streams, or threads sharing a device) race
+   and must be serialized by the caller.  Arguments and results as
+   qi8_quip_convert. */
+QI8_API int qi8_quip_convert_noalloc(const void* w, int w_dtype, int64_t M, int64_t N, const float* s_u,
+                                     const float* s_v, int store_transformed, int requant, int block,
+                                     int8_t* q_out, float* scale_out, float* dequant_out, void* stream);
+
 /* Original-space requantization of a weight W[M,N] (row stride ld_w) with the
    QuIP requant rule (converters/quip_int8.py:1614-1669): scale =
    max(amax/127, 1e-12), q = rint(w / scale) in [-127, 127]; QI8_REQ_ROW ->
