@@ -22,7 +22,8 @@
 //     accumulates acc += p * sa * sb in registers (int8_gemm semantics,
 //     comfy/int8_kernels.py:468-480).  The int32 -> fp32 conversion uses the
 //     exact 1.5*2^23 bias trick (|p| <= 128*128*128 < 2^22) so it costs one
-//     integer add and one packed fp32 add instead of a low-throughput I2F.
+//     integer add and one packed fp32 add instead of a low-throughput I2F;
+//     TMEM loads are software-pipelined 16 columns ahead of the arithmetic.
 //
 // Every mbarrier wait is bounded (globaltimer); on expiry the waiting role
 // sets a bit in the device status word and an abort flag in shared memory,
@@ -54,22 +55,25 @@ constexpr int EPI_REGS = 240;
 constexpr int CTRL_REGS = 24;
 static_assert(256 * EPI_REGS + 128 * CTRL_REGS == THREADS * LAUNCH_REGS, "register split must balance");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int STAGE_SCRATCH_BYTES = 3 * NUM_EPI_WARPS * 128 * 4;  // column scales, bias, per-kb scales
-constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
+// column scales, bias, per-kb scales (fp32 x 128 per warp each) + a 32x16 bf16 transpose tile per warp
+constexpr int STAGE_SCRATCH_BYTES = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 16 * 32 * 2;
+constexpr int NUM_BARS = 2 * STAGES + 8 + 1;  // full, empty, tfull[2][2], tempty[2][2], drain
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES + NUM_BARS * 8 + 16;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;  // 0.2 s when cleaning up
 
-// Block-scaled mode keeps every TMEM accumulator pre-loaded with the int32
-// bit pattern of 1.5*2^23 and always accumulates onto it: after the K block,
-// the bits read back are exactly the fp32 value 1.5*2^23 + partial (partial
-// magnitude <= 128*128*128 < 2^22), so one fp32 subtract recovers it.
+// Exact int32 -> fp32 of a K-block partial p (|p| <= 128*128*128 < 2^22):
+// the bits of 0x4B400000 + p are the fp32 value 1.5*2^23 + p, so one integer
+// add and one fp32 subtract convert it (instead of a low-throughput I2F).
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;
 constexpr float MAGIC_F = 12582912.0f;
 
 // instruction descriptor: D s32, A/B signed int8, both K-major, N=256, M=128
 constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                            ((uint32_t)(BM >> 4) << 24);
+// same with N = 128: the block-scaled kernel issues each K block as two column halves
+constexpr uint32_t IDESC_N128 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
 
 struct GemmArgs {
   int M, N, K, KB;
@@ -157,12 +161,13 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t accum) {
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t accum,
+                                          uint32_t idesc = IDESC) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(IDESC), "r"(accum)
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -177,22 +182,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-// Writes the same 32-bit value v into 16 consecutive columns of this warp's lanes.
-__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
 // Shared-memory float2 load that stays in program order with the tcgen05
 // asm statements around it (keeps scale registers from being hoisted).
 __device__ __forceinline__ float2 lds_f2(const float* p) {
@@ -200,15 +189,6 @@ __device__ __forceinline__ float2 lds_f2(const float* p) {
   asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(smem_u32(p)));
   return v;
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
 // 128 bytes, 8-row core groups 1024 bytes apart (SBO), sm_100 version bit.
@@ -341,6 +321,76 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
   return 1.0f;
 }
 
+// Tile epilogue of the block-scaled kernel: final scales, optional GELU and
+// the stores, from the 128 accumulator registers of one thread.
+// SWAP: thread = output feature rr, the 128 values are tokens cc0..cc0+127;
+// stores go through a per-warp 16x32 bf16 transpose tile so each lane writes
+// 32 contiguous bytes.  Otherwise: thread = token rr, values = features.
+template <bool SWAP, bool GELU>
+__device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&acc)[64], const float* my_col,
+                                              const float* my_bias, float frow, float brow, int rr, int cc0, int R,
+                                              int C, int warp, int lane, __nv_bfloat16* sxp) {
+  const bool row_ok = rr < R;
+  if constexpr (SWAP) {
+    __nv_bfloat16* tb = sxp + warp * (16 * 32);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int col0 = cc0 + c * 16;
+      if (col0 >= C) break;  // warp-uniform
+      if (p.out_dtype == QI8_BF16) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = c * 16 + j;
+          const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
+          float y = __fadd_rn(__fmul_rn(__fmul_rn(a, my_col[col]), frow), brow);
+          if (GELU) y = act_gelu(y, p.out_dtype);
+          tb[j * 32 + lane] = __float2bfloat16_rn(y);
+        }
+        __syncwarp();
+        const int t = lane >> 1, h = lane & 1;
+        const int tok = col0 + t;
+        const int f0 = rr - lane + h * 16;  // first of the 16 features this lane stores
+        if (tok < C && f0 < R) {
+          const uint4* src = reinterpret_cast<const uint4*>(tb + t * 32 + h * 16);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)tok * p.ld_out + f0);
+          dst[0] = src[0];
+          dst[1] = src[1];
+        }
+        __syncwarp();
+      } else if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = c * 16 + j;
+          const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
+          float y = __fadd_rn(__fmul_rn(__fmul_rn(a, my_col[col]), frow), brow);
+          if (GELU) y = act_gelu(y, p.out_dtype);
+          if (col0 + j < C) {
+            const int64_t o = (int64_t)(col0 + j) * p.ld_out + rr;
+            if (p.out_dtype == QI8_F16) static_cast<__half*>(p.out)[o] = __float2half_rn(y);
+            else static_cast<float*>(p.out)[o] = y;
+          }
+        }
+      }
+    }
+  } else {
+    if (!row_ok) return;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      const int n0 = cc0 + g * 8;
+      if (n0 >= C) break;
+      float y[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = g * 8 + j;
+        const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
+        y[j] = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), my_col[col]), my_bias[col]);
+        if (GELU) y[j] = act_gelu(y[j], p.out_dtype);
+      }
+      store_row8(p, rr, n0, y);
+    }
+  }
+}
+
 // SWAP: the weight tile is the MMA A operand (TMEM lanes = output features)
 // and the activation tile the B operand (TMEM columns = tokens).  Used when
 // the weight scale varies per (row, K block) and the activation scale does
@@ -358,14 +408,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   float* scol = reinterpret_cast<float*>(sb + STAGES * (A_BYTES + B_BYTES));  // [8 warps][128] column scales
   float* sbias = scol + NUM_EPI_WARPS * 128;                                   // [8 warps][128] bias
   float* skb = sbias + NUM_EPI_WARPS * 128;                                    // [8 warps][128] per-kb scales
+  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][16][32] transpose
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto full_bar = [&](int s) { return smem_u32(bars + s); };
   auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
-  auto tfull_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + b); };
-  auto tempty_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + 2 + b); };
-  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
+  // accumulator buffer b, column half h (the plain kernel uses half 0 for the whole buffer)
+  auto tfull_bar = [&](int b, int h) { return smem_u32(bars + 2 * STAGES + 2 * b + h); };
+  auto tempty_bar = [&](int b, int h) { return smem_u32(bars + 2 * STAGES + 4 + 2 * b + h); };
+  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -375,8 +427,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), NUM_EPI_WARPS);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(tfull_bar(b, h), 1);
+        mbar_init(tempty_bar(b, h), PROMOTE ? NUM_EPI_WARPS / 2 : NUM_EPI_WARPS);
+      }
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -397,21 +451,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int KB = p.KB;
-  if constexpr (PROMOTE) {
-    if (warp < NUM_EPI_WARPS) {
-      // pre-bias both accumulator buffers (this warp's lanes and columns)
-      const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
-#pragma unroll
-      for (int b = 0; b < 2; ++b)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) tmem_fill16(tmem_base + lb + (uint32_t)(b * BN + (warp >> 2) * 128 + c * 16), MAGIC_BITS);
-      tmem_wait_st();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
-
   if (warp >= NUM_EPI_WARPS) {
     // control warpgroup: producer, MMA issuer and two idle warps.  In the
     // block-scaled kernel it hands registers to the epilogue warpgroups.
@@ -457,32 +496,61 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         for (int u = 0; ok && u < n_units; ++u, ++au) {
           const int buf = au & 1;
-          if (!mbar_wait(tempty_bar(buf), ((au >> 1) & 1) ^ 1u, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem_base + (uint32_t)(buf * BN);
-          const int kb0 = PROMOTE ? u : 0, kb1 = PROMOTE ? u + 1 : KB;
-          for (int kb = kb0; kb < kb1; ++kb) {
+          const uint32_t tpar = ((au >> 1) & 1) ^ 1u;
+          if constexpr (PROMOTE) {
+            // one K block, issued as two N=128 halves so each epilogue
+            // warpgroup can start (and release) its half independently
             if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
               ok = false;
               break;
             }
-            tc_fence_after();
             const uint64_t da = sw128_desc(sA + s * A_BYTES);
-            const uint64_t db = sw128_desc(sB + s * B_BYTES);
 #pragma unroll
-            for (int k = 0; k < BK / 32; ++k)
-              tc_mma_i8(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k),
-                        (PROMOTE || kb > kb0 || k > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; ++h) {
+              if (!mbar_wait(tempty_bar(buf, h), tpar, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t d = tmem_base + (uint32_t)(buf * BN + h * 128);
+              const uint64_t db = sw128_desc(sB + s * B_BYTES + h * (128 * BK));
+#pragma unroll
+              for (int k = 0; k < BK / 32; ++k)
+                tc_mma_i8(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), k > 0 ? 1u : 0u, IDESC_N128);
+              tc_commit(tfull_bar(buf, h));
+            }
+            if (!ok) break;
             tc_commit(empty_bar(s));
             if (++s == STAGES) {
               s = 0;
               ph ^= 1u;
             }
+          } else {
+            if (!mbar_wait(tempty_bar(buf, 0), tpar, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+            for (int kb = 0; kb < KB; ++kb) {
+              if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t da = sw128_desc(sA + s * A_BYTES);
+              const uint64_t db = sw128_desc(sB + s * B_BYTES);
+#pragma unroll
+              for (int k = 0; k < BK / 32; ++k)
+                tc_mma_i8(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), (kb > 0 || k > 0) ? 1u : 0u);
+              tc_commit(empty_bar(s));
+              if (++s == STAGES) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+            if (ok) tc_commit(tfull_bar(buf, 0));
           }
-          if (ok) tc_commit(tfull_bar(buf));
         }
       }
       // all MMAs issued by this thread complete before TMEM is released
@@ -560,29 +628,33 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
           const float2 sk2 = make_float2(sk, sk);
-          if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
+          if (!mbar_wait(tfull_bar(buf, half), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const bool last = kb == KB - 1;
-#pragma unroll
-          for (int rnd = 0; rnd < 2; ++rnd) {
-            uint32_t r[4][16];
-            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128 + rnd * 64);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld16(ta + c * 16, r[c]);
-            tmem_wait_ld();
-            if (!last) {
-#pragma unroll
-              for (int c = 0; c < 4; ++c) tmem_fill16(ta + c * 16, MAGIC_BITS);  // re-bias for the next K block
-            }
+          // 4 chunks of 32 columns; the load of chunk c+1 is in flight while
+          // chunk c is promoted (tcgen05.wait::ld waits for all earlier loads)
+          {
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * BN + half * 128);
+            uint32_t rb[2][32];
+            tmem_ld32(ta, rb[0]);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
+              tmem_wait_ld();
+              if (c < 3) tmem_ld32(ta + (c + 1) * 32, rb[(c + 1) & 1]);
+              if (c == 3) {
+                // every column of this buffer half is in registers: release it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(buf, half));
+              }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int col = rnd * 64 + c * 16 + 2 * j;
-                float2 f = make_float2(__uint_as_float(r[c][2 * j]), __uint_as_float(r[c][2 * j + 1]));
+              for (int j = 0; j < 16; ++j) {
+                const int col = c * 32 + 2 * j;
+                // exact int32 -> fp32 (|p| < 2^22): bits(0x4B400000 + p) = 1.5*2^23 + p
+                float2 f = make_float2(__uint_as_float(rb[c & 1][2 * j] + MAGIC_BITS),
+                                       __uint_as_float(rb[c & 1][2 * j + 1] + MAGIC_BITS));
                 f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
                 float2 sc = sk2;
                 if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
@@ -590,74 +662,22 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
-          if (!last) {
-            // the last K block's buffer stays held for the tile epilogue below
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(buf));
-          }
         }
         if (!ok) break;
-        // ---- tile epilogue: final scales in registers, staged through the
-        // held TMEM buffer so the store loop below stays compact
-        const int bufl = (au - 1) & 1;
-        const uint32_t tl = tmem_base + lane_base + (uint32_t)(bufl * BN + half * 128);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int col = c * 16 + j;
-            const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
-            float y;
-            if constexpr (SWAP) y = __fadd_rn(__fmul_rn(__fmul_rn(a, my_col[col]), frow), brow);
-            else y = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), my_col[col]), my_bias[col]);
-            v[j] = __float_as_uint(y);
-          }
-          tmem_st16(tl + c * 16, v);
+        // ---- tile epilogue, straight from the registers (the TMEM buffer is
+        // already released, so the next tile's MMAs overlap these stores)
+        // SWAP transposes through shared memory with __syncwarp, so the whole
+        // warp enters together; lanes whose row is out of range store nothing
+        if (cols_ok && (SWAP || row_ok)) {
+          if (p.act == QI8_ACT_GELU) finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, R, C, warp, lane, sxp);
+          else finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, R, C, warp, lane, sxp);
         }
-        tmem_wait_st();
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          uint32_t v[16];
-          tmem_ld16(tl + c * 16, v);
-          tmem_wait_ld();
-          tmem_fill16(tl + c * 16, MAGIC_BITS);  // re-bias for the next tile
-          const int col0 = cc0 + c * 16;
-          if (!row_ok || col0 >= C) continue;
-          float y[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            y[j] = __uint_as_float(v[j]);
-            if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
-          }
-          if constexpr (SWAP) {
-            // thread = output feature rr; the 16 values are 16 consecutive tokens
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if (col0 + j < C) {
-                const int64_t o = (int64_t)(col0 + j) * p.ld_out + rr;
-                if (p.out_dtype == QI8_BF16) static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(y[j]);
-                else if (p.out_dtype == QI8_F16) static_cast<__half*>(p.out)[o] = __float2half_rn(y[j]);
-                else static_cast<float*>(p.out)[o] = y[j];
-              }
-            }
-          } else {
-            store_row8(p, rr, col0, *reinterpret_cast<const float(*)[8]>(&y[0]));
-            if (col0 + 8 < C) store_row8(p, rr, col0 + 8, *reinterpret_cast<const float(*)[8]>(&y[8]));
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(bufl));
       } else {
         const int m = rr;
         const int ncol0 = cc0;
         const float fa = frow;
         const int buf = au & 1;
-        if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
+        if (!mbar_wait(tfull_bar(buf, 0), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
           ok = false;
           break;
         }
@@ -672,7 +692,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (rnd == 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(buf));
+            if (lane == 0) mbar_arrive(tempty_bar(buf, 0));
           }
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
