@@ -404,8 +404,211 @@ __global__ void __launch_bounds__(256) quant_tile128_kernel(const T* __restrict_
   if (threadIdx.x == 0) scale[tr * nbc + tc] = s;
 }
 
+// ============================================ per-token quant, warps per row
+// The per-token path of the activation quantizer for 16-byte aligned rows:
+// W warps share one row (W in {1,2,4,8}, 8/W rows per 256-thread block),
+// every lane keeps CPL raw 16-byte chunks in registers so that all of a
+// row's loads are in flight at once, and the block loops over row groups
+// (persistent grid).  GELU rounds to T in place, so both passes read the
+// packed values.  Quantization is q = rint(v * rcp) with s = max(amax/127,
+// 1e-30) and rcp = 1/s (both correctly rounded, as the row kernel above):
+// |v * rcp| <= 127 * (1 + 3 ulp) rounds into [-127, 127], so the clamp is a
+// no-op and rint is done by adding 1.5 * 2^23 in fp32 (round to nearest
+// even), leaving the int8 in the low byte of the sum.
+namespace tok {
+
+template <typename T> struct Pack;
+template <> struct Pack<__nv_bfloat16> {
+  static constexpr int EPC = 8;  // elements per 16-byte chunk
+  __device__ static __forceinline__ float2 f2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  }
+  __device__ static __forceinline__ uint32_t from_f2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static __forceinline__ uint32_t absmax2(uint32_t m, uint32_t w) {
+    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&m), b = *reinterpret_cast<__nv_bfloat162*>(&w);
+    __nv_bfloat162 r = __hmax2(a, __habs2(b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  __device__ static __forceinline__ float fold(uint32_t m) { float2 f = f2(m); return fmaxf(f.x, f.y); }
+};
+template <> struct Pack<__half> {
+  static constexpr int EPC = 8;
+  __device__ static __forceinline__ float2 f2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<__half2*>(&w));
+  }
+  __device__ static __forceinline__ uint32_t from_f2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static __forceinline__ uint32_t absmax2(uint32_t m, uint32_t w) {
+    __half2 a = *reinterpret_cast<__half2*>(&m), b = *reinterpret_cast<__half2*>(&w);
+    __half2 r = __hmax2(a, __habs2(b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  __device__ static __forceinline__ float fold(uint32_t m) { float2 f = f2(m); return fmaxf(f.x, f.y); }
+};
+template <> struct Pack<float> {
+  static constexpr int EPC = 4;
+  // one fp32 per word; pairs of words form the float2 operands
+};
+
+__device__ __forceinline__ uint32_t bytes4(float2 a, float2 b) {
+  const uint32_t lo = __byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x0040);
+  const uint32_t hi = __byte_perm(__float_as_uint(b.x), __float_as_uint(b.y), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
+constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23
+
+// rint(fl(v * rcp)) + 1.5 * 2^23 for two values: separately rounded scalar
+// multiply and add (__fmul_rn / __fadd_rn are never merged into an fma).
+__device__ __forceinline__ float2 magic_q(float2 v, float rcp) {
+  return make_float2(__fadd_rn(__fmul_rn(v.x, rcp), RINT_MAGIC), __fadd_rn(__fmul_rn(v.y, rcp), RINT_MAGIC));
+}
+
+template <typename T, int CPL, bool GELU>
+__global__ void __launch_bounds__(256, 3) token_rows_kernel(QArgs a, int rows, int W) {
+  __shared__ float red[2][8];
+  constexpr int EPC = Pack<T>::EPC;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rpb = 8 / W, wr = warp % W, rsub = warp / W;
+  const int nc = a.n / EPC;
+  const int groups = (rows + rpb - 1) / rpb;
+  int it = 0;
+  for (int g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+    const int row = g * rpb + rsub;
+    const bool live = row < rows;
+    const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + (int64_t)row * a.ld_x);
+    uint4 x[CPL];
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = (i * W + wr) * 32 + lane;
+      x[i] = (live && c < nc) ? __ldcs(xr + c) : make_uint4(0, 0, 0, 0);
+    }
+    float amax;
+    if constexpr (sizeof(T) == 2) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(&x[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (GELU) {
+            const float2 f = Pack<T>::f2(w[j]);
+            w[j] = Pack<T>::from_f2(gelu_erf(f.x), gelu_erf(f.y));
+          }
+          m = Pack<T>::absmax2(m, w[j]);
+        }
+      }
+      amax = Pack<T>::fold(m);
+    } else {
+      amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        float* f = reinterpret_cast<float*>(&x[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (GELU) f[j] = gelu_erf(f[j]);
+          amax = fmaxf(amax, fabsf(f[j]));
+        }
+      }
+    }
+    amax = warp_max(amax);
+    if (W > 1) {
+      if (lane == 0) red[it & 1][warp] = amax;
+      __syncthreads();
+      amax = red[it & 1][rsub * W];
+      for (int k = 1; k < W; ++k) amax = fmaxf(amax, red[it & 1][rsub * W + k]);
+    }
+    if (!live) continue;
+    const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float rcp = __frcp_rn(s);
+    int8_t* qr = a.q + (int64_t)row * a.ld_q;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = (i * W + wr) * 32 + lane;
+      if (c < nc) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&x[i]);
+        if constexpr (sizeof(T) == 2) {
+          float2 f[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) f[j] = magic_q(Pack<T>::f2(w[j]), rcp);
+          *reinterpret_cast<uint2*>(qr + (int64_t)c * EPC) = make_uint2(bytes4(f[0], f[1]), bytes4(f[2], f[3]));
+        } else {
+          const float2 f0 = magic_q(make_float2(__uint_as_float(w[0]), __uint_as_float(w[1])), rcp);
+          const float2 f1 = magic_q(make_float2(__uint_as_float(w[2]), __uint_as_float(w[3])), rcp);
+          *reinterpret_cast<uint32_t*>(qr + (int64_t)c * EPC) = bytes4(f0, f1);
+        }
+      }
+    }
+    if (wr == 0 && lane == 0) a.scale[row] = s;
+  }
+}
+
+// (W, CPL) for a row of nc chunks: the fewest warps whose lanes hold the row
+// in at most 12 chunks each; 0 if the row is too wide.
+inline void choose_shape(int nc, int& W, int& cpl) {
+  static const int allowed[] = {1, 2, 3, 4, 6, 8, 12};
+  for (W = 1; W <= 8; W *= 2) {
+    const int need = (nc + 32 * W - 1) / (32 * W);
+    if (need <= 12) {
+      for (int c : allowed)
+        if (c >= need) { cpl = c; return; }
+    }
+  }
+  W = 0; cpl = 0;
+}
+
+template <typename T, int CPL, bool GELU>
+int launch_cpl(const QArgs& a, int rows, int W, cudaStream_t st) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, token_rows_kernel<T, CPL, GELU>, 256, 0) != cudaSuccess || b < 1)
+      b = 1;
+    per_sm = b;
+  }
+  const int rpb = 8 / W;
+  const int64_t groups = (rows + rpb - 1) / rpb;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  const unsigned grid = (unsigned)(groups < cap ? groups : (cap > 0 ? cap : 1));
+  token_rows_kernel<T, CPL, GELU><<<grid, 256, 0, st>>>(a, rows, W);
+  return check_cuda(cudaGetLastError(), "token_rows_kernel launch");
+}
+
+// Returns -1 when the row shape is outside this path (caller falls back).
+template <typename T, bool GELU>
+int launch(const QArgs& a, int64_t rows, cudaStream_t st) {
+  constexpr int EPC = Pack<T>::EPC;
+  if (!a.vec || a.n % EPC != 0 || rows >= (int64_t(1) << 31) || (a.ld_x * (int64_t)sizeof(T)) % 16 != 0 ||
+      a.ld_q % EPC != 0)
+    return -1;
+  int W, cpl;
+  choose_shape(a.n / EPC, W, cpl);
+  const int r = (int)rows;
+  switch (cpl) {
+    case 1: return launch_cpl<T, 1, GELU>(a, r, W, st);
+    case 2: return launch_cpl<T, 2, GELU>(a, r, W, st);
+    case 3: return launch_cpl<T, 3, GELU>(a, r, W, st);
+    case 4: return launch_cpl<T, 4, GELU>(a, r, W, st);
+    case 6: return launch_cpl<T, 6, GELU>(a, r, W, st);
+    case 8: return launch_cpl<T, 8, GELU>(a, r, W, st);
+    case 12: return launch_cpl<T, 12, GELU>(a, r, W, st);
+    default: return -1;
+  }
+}
+
+}  // namespace tok
+
 template <typename T, int MODE, bool GELU>
 int launch_quant_rows_T(const QArgs& a, int64_t rows, cudaStream_t st) {
+  if constexpr (MODE == QI8_Q_TOKEN) {
+    const int rc = tok::launch<T, GELU>(a, rows, st);
+    if (rc >= 0) return rc;
+  }
   const int nc = (a.n + 7) / 8;
   const int cpt = (nc + QR_THREADS - 1) / QR_THREADS;
   if (a.n % 8 != 0 || !a.vec) {

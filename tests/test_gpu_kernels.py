@@ -94,7 +94,7 @@ def test_quant_rows_token_golden(golden):
     g = golden("act_token.npz")
     q, s = ops.quant_rows(bf16_cu(g["xa_bf16"]))
     assert np.array_equal(np_(q), g["qa"]) and np.array_equal(np_(s), g["sa"])
-    q, s = ops.quant_rows(cu(g["xb"]))  # n = 1000: scalar path
+    q, s = ops.quant_rows(cu(g["xb"]))  # n = 1000
     assert np.array_equal(np_(q), g["qb"]) and np.array_equal(np_(s), g["sb"])
 
 
@@ -110,7 +110,22 @@ def test_quant_rows_token_random(n, dtype):
     assert np.array_equal(np_(q), qr) and np.array_equal(np_(s), sr)
 
 
-@pytest.mark.parametrize("n", [3072, 12288, 1000])
+@pytest.mark.parametrize("n,rows", [(3072, 3000), (12288, 2049), (24576, 300)])
+def test_quant_rows_token_many_rows(n, rows):
+    # more row groups than resident blocks: the persistent loop, plus a zero
+    # row and a one-hot row
+    r = rng(n + rows)
+    x = (r.standard_normal((rows, n)) * 2).astype(np.float32)
+    x[5] = 0.0
+    x[7] = 0.0
+    x[7, n - 1] = -3.0
+    xt = torch.from_numpy(x).to(torch.bfloat16)
+    q, s = ops.quant_rows(xt.to(dev()))
+    qr, sr = O.quantize_int8_axiswise(xt.float().numpy())
+    assert np.array_equal(np_(q), qr) and np.array_equal(np_(s), sr)
+
+
+@pytest.mark.parametrize("n", [3072, 12288, 1000, 24576])
 def test_quant_rows_gelu_fused(n):
     # GELU between the DiT MLP projections: torch gelu on the bf16 tensor, then per-token quant
     r = rng(n + 1)
