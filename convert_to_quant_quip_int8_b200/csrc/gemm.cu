@@ -4,15 +4,21 @@
 //   checkpoint layout of the reference's weights, so no per-call transpose
 //   copy as in comfy/quant_ops.py:471)
 //
-// One persistent CTA per SM, warp-specialized:
-//   warp 8      TMA producer: 128x128 (A) and 256x128 (B) int8 tiles, 128-byte
-//               swizzle, 4-stage mbarrier ring (48 KB / stage)
+// Two persistent, warp-specialized kernels share the roles:
+//   warp 8      TMA producer (128-byte swizzle, mbarrier stage ring)
 //   warp 9      TMEM allocator + single-thread tcgen05.mma.kind::i8 issuer
-//               (M=128, N=256, K=32 per instruction, s32 accumulators)
 //   warps 0..7  epilogue: tcgen05.ld from TMEM (warp w reads lane quadrant
 //               w%4, column half w/4), scaling, bias, activation, store
-// TMEM holds two 128x256 s32 accumulator buffers (all 512 columns), so the
-// MMA of the next accumulation unit overlaps the epilogue of the current one.
+//   warps 10,11 only donate registers to the epilogue (block-scaled kernels)
+//
+// * gemm_pair_kernel (used whenever the TMEM-lane operand has more than 128
+//   rows): CTA pairs of a 2-CTA cluster issue tcgen05.mma.cta_group::2 with
+//   M=256, N=256, K=32; each CTA loads 128 rows of A and 128 rows of B per
+//   K block (32 KB, 6-stage ring) and holds its 128 output rows in two
+//   256-column TMEM buffers.  Per SM this loads a third less operand data
+//   from L2 than a single-CTA 128x256 tile for the same MMA work.
+// * gemm_i8_kernel: one CTA per 128x256 tile (M=128, N=256), for operands
+//   of at most 128 TMEM-lane rows.
 //
 // Accumulation units:
 //   * plain epilogue (tensor / row / no scales): one unit per output tile,
@@ -22,13 +28,14 @@
 //     accumulates acc += p * sa * sb in registers (int8_gemm semantics,
 //     comfy/int8_kernels.py:468-480).  The int32 -> fp32 conversion uses the
 //     exact 1.5*2^23 bias trick (|p| <= 128*128*128 < 2^22) so it costs one
-//     integer add and one packed fp32 add instead of a low-throughput I2F;
-//     TMEM loads are software-pipelined 16 columns ahead of the arithmetic.
+//     integer add and half a packed fp32 add instead of a low-throughput
+//     I2F; TMEM loads of the next 32 columns are in flight during the math.
 //
 // Every mbarrier wait is bounded (globaltimer); on expiry the waiting role
 // sets a bit in the device status word and an abort flag in shared memory,
 // all roles leave their loops, in-flight TMA copies and MMAs are waited for
-// (again bounded) and TMEM is freed before the CTA exits.
+// (again bounded) and TMEM is freed before the CTA exits (the CTA pair meets
+// at a cluster barrier first).
 #include <cuda.h>
 #include <cstdint>
 
@@ -321,22 +328,24 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
   return 1.0f;
 }
 
-// Tile epilogue of the block-scaled kernel: final scales, optional GELU and
-// the stores, from the 128 accumulator registers of one thread.
+// Tile epilogue of the block-scaled kernels: final scales, optional GELU and
+// the stores, from the WC accumulator registers of one thread.
 // SWAP: thread = output feature rr, the 128 values are tokens cc0..cc0+127;
 // stores go through a per-warp 16x32 bf16 transpose tile so each lane writes
 // 32 contiguous bytes.  Otherwise: thread = token rr, values = features.
-template <bool SWAP, bool GELU>
-__device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&acc)[64], const float* my_col,
-                                              const float* my_bias, float frow, float brow, int rr, int cc0, int R,
-                                              int C, int warp, int lane, __nv_bfloat16* sxp) {
+template <bool SWAP, bool GELU, int WC = 128>
+__device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&acc)[WC / 2], const float* my_col,
+                                              const float* my_bias, float frow, float brow, int rr, int cc0, int cc1,
+                                              int R, int C, int warp, int lane, __nv_bfloat16* sxp) {
+  // accumulator column j < WC/2 is output column cc0 + j, column j >= WC/2 is cc1 + j - WC/2
+  constexpr int RUN = WC / 2;
   const bool row_ok = rr < R;
   if constexpr (SWAP) {
     __nv_bfloat16* tb = sxp + warp * (16 * 32);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int col0 = cc0 + c * 16;
-      if (col0 >= C) break;  // warp-uniform
+    for (int c = 0; c < WC / 16; ++c) {
+      const int col0 = c * 16 < RUN ? cc0 + c * 16 : cc1 + c * 16 - RUN;
+      if (col0 >= C) continue;  // warp-uniform
       if (p.out_dtype == QI8_BF16) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -375,9 +384,9 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
   } else {
     if (!row_ok) return;
 #pragma unroll
-    for (int g = 0; g < 16; ++g) {
-      const int n0 = cc0 + g * 8;
-      if (n0 >= C) break;
+    for (int g = 0; g < WC / 8; ++g) {
+      const int n0 = g * 8 < RUN ? cc0 + g * 8 : cc1 + g * 8 - RUN;
+      if (n0 >= C) continue;
       float y[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -669,8 +678,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         // SWAP transposes through shared memory with __syncwarp, so the whole
         // warp enters together; lanes whose row is out of range store nothing
         if (cols_ok && (SWAP || row_ok)) {
-          if (p.act == QI8_ACT_GELU) finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, R, C, warp, lane, sxp);
-          else finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, R, C, warp, lane, sxp);
+          if (p.act == QI8_ACT_GELU)
+            finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
+          else
+            finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
         }
       } else {
         const int m = rr;
@@ -727,6 +738,397 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ============================================== CTA-pair kernel (cta_group::2)
+// Two CTAs of a cluster share each MMA: tcgen05.mma.cta_group::2 with M=256
+// reads the A rows of each CTA (128 each) and the B rows of both CTAs (BNP/2
+// each) from their own shared memory, and writes each CTA's 128 output rows
+// into that CTA's TMEM.  Per SM this halves the B tile that has to be
+// loaded and read from shared memory for the same MMA work, or (BNP = 128)
+// keeps the traffic of the single-CTA 128x256 tile while giving four
+// accumulator buffers instead of two.
+//   * both producers load their halves; the pair's stage barrier lives in
+//     the even CTA (the leader), which alone arms it with the bytes of both;
+//   * the leader's warp 9 lane 0 issues the MMAs; its commits arrive on the
+//     stage-empty and accumulator-full barriers of both CTAs (multicast
+//     commit; no multicast loads are used anywhere);
+//   * both CTAs' epilogue warps release an accumulator buffer by arriving on
+//     the leader's accumulator-empty barrier (16 arrivals).
+// Every wait is bounded as in the single-CTA kernel; both CTAs meet at a
+// cluster barrier before the TMEM is freed and the CTAs exit.
+namespace pairk {
+
+// Pair tile: 256 TMEM-lane rows (128 per CTA) x 256 columns (each CTA loads
+// 128 of the column operand's rows; the MMA reads both halves).
+constexpr int PBN = 256;
+constexpr int B_HALF = PBN / 2;
+constexpr int P_A_BYTES = 128 * BK;
+constexpr int P_B_BYTES = B_HALF * BK;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;  // 32 KB per CTA
+constexpr int P_STAGES = 6;
+constexpr int P_BUFS = 2;  // TMEM accumulator buffers of 256 columns
+// M = 256 (pair), N = 256
+constexpr uint32_t IDESC_P256 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                                ((uint32_t)(256 >> 4) << 24);
+constexpr int P_NUM_BARS = 2 * P_STAGES + 2 * P_BUFS + 1;  // full, empty, tfull, tempty, drain
+constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 16 * 32 * 2;
+constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + P_SCRATCH + P_NUM_BARS * 8 + 16;
+static_assert(P_SMEM <= 232448, "shared memory");
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of either CTA of the pair.  Default semantics
+// (release at CTA scope): the TMEM reads it publishes are ordered by
+// tcgen05.wait::ld + tcgen05.fence::before_thread_sync, and a cluster-scope
+// release would also wait for this thread's outstanding global loads.
+__device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on a
+// barrier of either CTA of the pair (bar is a shared::cluster address)
+__device__ __forceinline__ void tma_load_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// arrive on the barrier at offset `bar` of every CTA in `mask` once all
+// earlier MMAs of this thread have completed
+__device__ __forceinline__ void commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+               "h"(mask)
+               : "memory");
+}
+
+// One accumulation unit per K block (block-scaled) or per tile (plain), in
+// TMEM buffer (unit % 2); each epilogue warp drains 32 lanes x 128 columns.
+template <bool PROMOTE, bool SWAP>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sb = smem_raw + (base - raw);
+  const uint32_t sA = base;
+  const uint32_t sB = base + P_STAGES * P_A_BYTES;
+  float* scol = reinterpret_cast<float*>(sb + P_STAGES * P_STAGE_BYTES);  // [8 warps][128] column scales
+  float* sbias = scol + NUM_EPI_WARPS * 128;                              // [8 warps][128] bias
+  float* skb = sbias + NUM_EPI_WARPS * 128;                               // [8 warps][128] per-kb scales
+  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][16][32]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + P_STAGES * P_STAGE_BYTES + P_SCRATCH);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P_NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + P_STAGES + s); };
+  auto tfull_bar = [&](int b) { return smem_u32(bars + 2 * P_STAGES + b); };
+  auto tempty_bar = [&](int b) { return smem_u32(bars + 2 * P_STAGES + P_BUFS + b); };
+  const uint32_t drain_bar = smem_u32(bars + 2 * P_STAGES + 2 * P_BUFS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < P_BUFS; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 2 * NUM_EPI_WARPS);  // every epilogue warp of both CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  if (warp == PRODUCER_WARP && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  // barriers initialised and TMEM allocated in both CTAs before any peer access
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int KB = p.KB;
+  const int r_ptiles = p.r_tiles;  // tiles of 256 rows over the TMEM-lane operand
+  if (warp >= NUM_EPI_WARPS) {
+    if constexpr (PROMOTE) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CTRL_REGS));
+    if (warp == PRODUCER_WARP) {
+      if (lane == 0) {
+        const uint32_t full0 = mapa(full_bar(0), 0);
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
+          const int r0 = (tile % r_ptiles) * 256 + (int)rank * 128;
+          const int c0 = (tile / r_ptiles) * PBN + (int)rank * B_HALF;
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.status, ST_GEMM_PRODUCER, WAIT_LIMIT_NS)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * P_STAGE_BYTES);
+            const uint32_t fb = full0 + (uint32_t)(s * 8);
+            tma_load_pair(sA + s * P_A_BYTES, &tmA, kb * BK, r0, fb);
+            tma_load_pair(sB + s * P_B_BYTES, &tmB, kb * BK, c0, fb);
+            if (++s == P_STAGES) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+      }
+    } else if (warp == MMA_WARP) {
+      if (leader && lane == 0) {
+        int s = 0;
+        uint32_t ph = 0;
+        int u = 0;  // accumulation units issued (one per K block, or one per tile)
+        bool ok = true;
+        const int n_units = PROMOTE ? KB : 1;
+        for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
+          for (int w = 0; ok && w < n_units; ++w, ++u) {
+            const int buf = u & 1;
+            if (!mbar_wait(tempty_bar(buf), ((u >> 1) & 1) ^ 1u, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem_base + (uint32_t)(buf * PBN);
+            const int kb_n = PROMOTE ? 1 : KB;
+            for (int kb = 0; kb < kb_n; ++kb) {
+              if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t da = sw128_desc(sA + s * P_A_BYTES);
+              const uint64_t db = sw128_desc(sB + s * P_B_BYTES);
+#pragma unroll
+              for (int k = 0; k < BK / 32; ++k)
+                mma_pair(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC_P256, (kb > 0 || k > 0) ? 1u : 0u);
+              commit_pair(empty_bar(s), 3);
+              if (++s == P_STAGES) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+            if (!ok) break;
+            commit_pair(tfull_bar(buf), 3);
+          }
+        }
+        // every MMA of this thread completes before the cluster barrier below
+        commit_pair(drain_bar, 1);
+        if (ok) mbar_wait(drain_bar, 0, abort_flag, p.status, ST_GEMM_DRAIN, WAIT_LIMIT_NS);
+        else drain_wait(drain_bar, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------- epilogue
+    if constexpr (PROMOTE) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(EPI_REGS));
+    const int quad = warp & 3, cg = warp >> 2;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float* my_col = scol + warp * 128;
+    float* my_bias = sbias + warp * 128;
+    float* my_kb = skb + warp * 128;
+    const int R = SWAP ? p.N : p.M;
+    const int C = SWAP ? p.M : p.N;
+    const uint32_t tempty0 = mapa(tempty_bar(0), 0);
+    int au = 0;
+    bool ok = true;
+    for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
+      const int rr = (tile % r_ptiles) * 256 + (int)rank * 128 + quad * 32 + lane;
+      const int c0 = (tile / r_ptiles) * PBN;
+      // this warp's 128 accumulator columns (output columns cc0 .. cc0 + 127)
+      const int cc0 = c0 + cg * 128;
+      const int cc1 = cc0 + 64;
+      const bool row_ok = rr < R;
+      const bool cols_ok = cc0 < C;
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int j = c * 32 + lane;
+        const int cc = j < 64 ? cc0 + j : cc1 + j - 64;
+        if constexpr (SWAP) {
+          my_col[j] = cc < C ? row_scale(p.a_scale, p.a_kind, cc) : 0.0f;
+        } else {
+          my_col[j] = cc < C ? row_scale(p.b_scale, p.b_kind, cc) : 0.0f;
+          my_bias[j] = (p.bias && cc < C) ? load_as_f32(p.bias, p.bias_dtype, cc) : 0.0f;
+        }
+      }
+      __syncwarp();
+      float frow = 1.0f, brow = 0.0f;
+      if (row_ok) {
+        if constexpr (SWAP) {
+          frow = row_scale(p.b_scale, p.b_kind, rr);
+          if (p.bias) brow = load_as_f32(p.bias, p.bias_dtype, rr);
+        } else {
+          frow = row_scale(p.a_scale, p.a_kind, rr);
+        }
+      }
+      if constexpr (PROMOTE) {
+        float2 acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        const bool a_kb = !SWAP && p.a_kind == QI8_S_ROW_KBLOCK;
+        const bool b_col = !SWAP && p.b_kind == QI8_S_ROW_KBLOCK;
+        const bool b_tile = p.b_kind == QI8_S_TILE128;
+        // SWAP: this row's K-block weight scales, loaded two K blocks ahead
+        const float* srow = p.b_scale + (int64_t)(row_ok ? rr : 0) * KB;
+        float sk_n1 = 0.0f, sk_n2 = 0.0f;
+        if constexpr (SWAP) {
+          sk_n1 = row_ok ? __ldg(srow) : 0.0f;
+          sk_n2 = (row_ok && KB > 1) ? __ldg(srow + 1) : 0.0f;
+        }
+        for (int kb = 0; kb < KB; ++kb, ++au) {
+          const int buf = au & 1;
+          // scale of the first and of the second 64-column run
+          float sk0 = 1.0f, sk1 = 1.0f;
+          if constexpr (SWAP) {
+            sk0 = sk1 = sk_n1;
+            sk_n1 = sk_n2;
+            sk_n2 = (row_ok && kb + 2 < KB) ? __ldg(srow + kb + 2) : 0.0f;
+          } else {
+            if (a_kb) sk0 = sk1 = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
+            if (b_tile) {
+              sk0 = __fmul_rn(sk0, cc0 < C ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f);
+              sk1 = __fmul_rn(sk1, cc1 < C ? __ldg(p.b_scale + (int64_t)(cc1 >> 7) * KB + kb) : 0.0f);
+            }
+            if (b_col) {
+              __syncwarp();
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const int j = c * 32 + lane;
+                const int n = j < 64 ? cc0 + j : cc1 + j - 64;
+                my_kb[j] = n < p.N ? __ldg(p.b_scale + (int64_t)n * KB + kb) : 0.0f;
+              }
+              __syncwarp();
+            }
+          }
+          if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          {
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * 128);
+            uint32_t rb[2][32];
+            tmem_ld32(ta, rb[0]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              tmem_wait_ld();
+              if (c < 3) tmem_ld32(ta + (c + 1) * 32, rb[(c + 1) & 1]);
+              if (c == 3) {
+                // every column of this warp's share is in registers: release the buffer
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) arrive_cluster(tempty0 + (uint32_t)(buf * 8));
+              }
+              const float skc = c < 2 ? sk0 : sk1;
+              const float2 sk2 = make_float2(skc, skc);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int col = c * 32 + 2 * j;
+                // exact int32 -> fp32 (|p| < 2^22): bits(0x4B400000 + p) = 1.5*2^23 + p
+                float2 f = make_float2(__uint_as_float(rb[c & 1][2 * j] + MAGIC_BITS),
+                                       __uint_as_float(rb[c & 1][2 * j + 1] + MAGIC_BITS));
+                f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
+                float2 sc = sk2;
+                if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
+                acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+              }
+            }
+          }
+        }
+        if (!ok) break;
+        if (cols_ok && (SWAP || row_ok)) {
+          if (p.act == QI8_ACT_GELU)
+            finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
+          else
+            finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
+        }
+      } else {
+        const int buf = au & 1;
+        if (!mbar_wait(tfull_bar(buf), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int rnd = 0; rnd < 2; ++rnd) {
+          uint32_t r[2][32];
+          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * 128 + rnd * 64);
+          tmem_ld32(ta, r[0]);
+          tmem_ld32(ta + 32, r[1]);
+          tmem_wait_ld();
+          if (rnd == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(tempty0 + (uint32_t)(buf * 8));
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int cc = rnd * 64 + c * 32;
+            const int n0 = cc0 + cc;
+            if (!row_ok || n0 >= p.N) continue;
+            if (p.out_dtype == QI8_I32) {
+              store_row32_i32(p, rr, n0, r[c]);
+            } else {
+              float y[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                // optimized_linear: res.float() * (x_s * w_s) + bias  (comfy/quant_ops.py:472-473)
+                y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(frow, my_col[cc + j]));
+                if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
+                if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
+              }
+              store_row32(p, rr, n0, y);
+            }
+          }
+        }
+        ++au;
+      }
+    }
+  }
+
+  // no CTA of the pair frees TMEM or exits while the other may still touch it
+  tc_fence_before();
+  cluster_sync();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+}  // namespace pairk
+
 // --------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -760,6 +1162,49 @@ int make_map(CUtensorMap* map, const int8_t* ptr, int64_t rows, int64_t K, uint3
 }
 
 bool g_attr_set[3][64];
+
+// Launches the CTA-pair kernel; grid = 2 x min(tiles, co-resident clusters).
+template <bool PROMOTE, bool SWAP>
+int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, int dev, cudaStream_t st) {
+  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP>;
+  static int max_clusters[64];
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (max_clusters[dev] == 0) {
+    QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pairk::P_SMEM));
+    if (PROMOTE) {
+      cudaFuncAttributes fa{};
+      QI8_CUDA(cudaFuncGetAttributes(&fa, kern));
+      QI8_REQUIRE(fa.numRegs == LAUNCH_REGS, QI8_EUNSUPPORTED,
+                  "block-scaled GEMM compiled with %d registers per thread, register split needs %d", fa.numRegs,
+                  LAUNCH_REGS);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (sm_count() > 0 ? sm_count() / 2 : 74), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = pairk::P_SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    QI8_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    QI8_REQUIRE(n > 0, QI8_EUNSUPPORTED, "no CTA pair of the GEMM fits on the device");
+    max_clusters[dev] = n;
+  }
+  const int ncl = p.num_tiles < max_clusters[dev] ? p.num_tiles : max_clusters[dev];
+  kern<<<2 * ncl, THREADS, pairk::P_SMEM, st>>>(mapA, mapB, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, kern);
+    return fail(QI8_ECUDA, "gemm_pair_kernel launch: %s (regs=%d smem=%d clusters=%d)", cudaGetErrorString(e),
+                fa.numRegs, pairk::P_SMEM, ncl);
+  }
+  return QI8_OK;
+}
 
 }  // namespace
 }  // namespace qi8
@@ -800,6 +1245,30 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   const int8_t* Rop = swap ? B : A;
   const int8_t* Cop = swap ? A : B;
   const int64_t Rrows = swap ? N : M, Crows = swap ? M : N;
+  int dev = 0;
+  QI8_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (Rrows > BM) {
+    // CTA pairs: 256 rows on TMEM lanes x 256 columns per pair tile
+    GemmArgs p{};
+    const int bnp = pairk::PBN;
+    p.M = (int)M; p.N = (int)N; p.K = (int)K; p.KB = (int)((K + BK - 1) / BK);
+    p.r_tiles = (int)((Rrows + 255) / 256);
+    p.c_tiles = (int)((Crows + bnp - 1) / bnp);
+    p.num_tiles = p.r_tiles * p.c_tiles;
+    p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
+    p.bias = bias; p.bias_dtype = bias_dtype; p.out = out; p.out_dtype = out_dtype; p.ld_out = ld_out;
+    p.act = act;
+    p.status = device_status_ptr();
+    CUtensorMap mapA, mapB;
+    int rc = make_map(&mapA, Rop, Rrows, K, 128);
+    if (rc) return rc;
+    rc = make_map(&mapB, Cop, Crows, K, bnp / 2);
+    if (rc) return rc;
+    if (!promote) return launch_pair<false, false>(mapA, mapB, p, dev, st);
+    if (swap) return launch_pair<true, true>(mapA, mapB, p, dev, st);
+    return launch_pair<true, false>(mapA, mapB, p, dev, st);
+  }
   CUtensorMap mapA, mapB;
   int rc = make_map(&mapA, Rop, Rrows, K, BM);
   if (rc) return rc;
@@ -816,8 +1285,6 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   p.act = act;
   p.status = device_status_ptr();
 
-  int dev = 0;
-  QI8_CUDA(cudaGetDevice(&dev));
   auto kern = !promote ? gemm_i8_kernel<false, false> : (swap ? gemm_i8_kernel<true, true> : gemm_i8_kernel<true, false>);
   const int variant = !promote ? 0 : (swap ? 2 : 1);
   if (dev < 64 && !g_attr_set[variant][dev]) {
