@@ -37,6 +37,23 @@ UNIT = "TOPS"
 L2_NOTE = "inputs larger than L2: per-step footprint ~280 MB (x 25 MB, W1+W2 75 MB, h 100 MB + 50 MB, y 25 MB) > 126 MB"
 
 
+PROFILE_GEMM = os.path.join(ROOT, "profiles", "gemm_pair_kernel_block_dit_mlp.md")
+
+
+def profiled_traffic():
+    """DRAM bytes per GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum,
+    averaged over the W1 and W2 launches) from the committed ncu summary of
+    this workload, or None when the summary is absent."""
+    try:
+        with open(PROFILE_GEMM) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -331,8 +348,9 @@ def main():
                 "path": "F.linear(x, QuantizedTensor W1) -> F.gelu -> F.linear(., W2), pinned host in/out",
                 "rel_err_vs_device_path": rel},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
-                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": None,
-                     "kernel": "gemm_i8_kernel<PROMOTE> (both GEMMs, CUDA events on the launch stream)",
+                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": profiled_traffic(),
+                     "traffic_note": "DRAM bytes per GEMM launch from ncu (profiles/gemm_pair_kernel_block_dit_mlp.md)",
+                     "kernel": "gemm_pair_kernel<PROMOTE,SWAP> (both GEMMs, CUDA events on the launch stream)",
                      "peak_note": f"dense int8 = 2 x {peak_kind} cuBLAS bf16 burst ({peaks.get('bf16_tflops')} TF/s)",
                      "per_gemm_ms": {"w1_gelu": round(statistics.mean(g1), 4), "w2": round(statistics.mean(g2), 4)}},
         "gpu_launches": launches_per_step * args.steps,
