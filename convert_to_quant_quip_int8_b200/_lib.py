@@ -62,6 +62,8 @@ SIGNATURES = {
     "qi8_quip_convert": (_I, [_P, _I, _I64, _I64, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I64, _P]),
     "qi8_quip_convert_noalloc": (_I, [_P, _I, _I64, _I64, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "qi8_requant_weight": (_I, [_P, _I, _I64, _I64, _I64, _I, _I, _P, _P, _P, _I64, _P]),
+    "qi8_weight_rotate2d": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _I64, _P]),
+    "qi8_allgather_cols": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
 }
 
 _lib = None

@@ -65,7 +65,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         objs.append(obj)
     tmp = LIB + ".tmp"
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
-           *objs, "-o", tmp]
+           *objs, "-ldl", "-o", tmp]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

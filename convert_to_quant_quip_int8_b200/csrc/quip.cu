@@ -414,6 +414,44 @@ int qi8_quip_convert_noalloc(const void* w, int w_dtype, int64_t M, int64_t N, c
                           dequant_out, scratch, NOALLOC_BYTES, stream);
 }
 
+int qi8_weight_rotate2d(const void* w, int w_dtype, int64_t M, int64_t N, int64_t M_pad, int64_t N_pad,
+                        const float* s_u, const float* s_v, int inverse, float* out, void* workspace,
+                        int64_t workspace_bytes, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(w && s_u && s_v && out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(w_dtype == QI8_BF16 || w_dtype == QI8_F16 || w_dtype == QI8_F32, QI8_EDTYPE, "weight dtype %d", w_dtype);
+  const int LM = log2_exact(M_pad), LN = log2_exact(N_pad);
+  QI8_REQUIRE(LM >= 0 && LM <= 15 && LN >= 1 && LN <= 15, QI8_ESHAPE,
+              "padded sizes must be powers of two (rows <= 32768, 2 <= cols <= 32768), got %lld x %lld",
+              (long long)M_pad, (long long)N_pad);
+  QI8_REQUIRE(M > 0 && N > 0 && M <= M_pad && N <= N_pad, QI8_ESHAPE, "bad sizes M=%lld N=%lld (padded %lld x %lld)",
+              (long long)M, (long long)N, (long long)M_pad, (long long)N_pad);
+  QI8_REQUIRE(aligned16(out), QI8_EALIGN, "out must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ColArgs ca{};
+  ca.w_dtype = w_dtype; ca.M = M; ca.N = N; ca.M_pad = M_pad; ca.N_pad = N_pad;
+  ca.s_u = s_u; ca.s_v = s_v;
+  ca.norm = (float)(1.0 / std::sqrt((double)M_pad));
+  if (!inverse) {
+    // out [M_pad, N_pad] = FHT_N(FHT_M(pad(W) * s_u * s_v^T)): the column
+    // passes load W with the signs, then one in-place FWHT per row
+    ca.w = w; ca.x = out; ca.ld_x = N_pad;
+    int rc = col_passes(true, ca, st);
+    if (rc) return rc;
+    return qi8_fwht_rows(out, QI8_F32, M_pad, N_pad, N_pad, N_pad, nullptr, nullptr, 1, out, stream);
+  }
+  // out [M, N] = slice(FHT_M(FHT_N(W')) * s_u * s_v^T) for W' [M_pad, N_pad]:
+  // row FWHTs into the workspace, then the column passes apply the signs and slice
+  QI8_REQUIRE(workspace && workspace_bytes >= M_pad * N_pad * 4, QI8_EINVAL,
+              "inverse rotation needs an fp32 workspace of M_pad * N_pad elements");
+  QI8_REQUIRE(aligned16(workspace), QI8_EALIGN, "workspace must be 16-byte aligned");
+  float* X = static_cast<float*>(workspace);
+  int rc = qi8_fwht_rows(w, w_dtype, M_pad, N_pad, N_pad, N_pad, nullptr, nullptr, 1, X, stream);
+  if (rc) return rc;
+  ca.w = nullptr; ca.x = X; ca.ld_x = N_pad; ca.dst = out; ca.ld_dst = N;
+  return col_passes(false, ca, st);
+}
+
 int qi8_requant_weight(const void* w, int w_dtype, int64_t M, int64_t N, int64_t ld_w, int requant, int block,
                        int8_t* q_out, float* scale_out, void* workspace, int64_t workspace_bytes, void* stream) {
   QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");

@@ -6,6 +6,7 @@ never allocates); every launch goes on ``torch.cuda.current_stream()``.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Optional, Tuple
 
@@ -235,6 +236,55 @@ def quip_convert(w: torch.Tensor, s_u: torch.Tensor, s_v: torch.Tensor, store_tr
                                  requant, block, L.ptr(q), L.ptr(s), L.ptr(deq), L.ptr(workspace), workspace.numel(),
                                  L.stream_ptr(w.device)), "qi8_quip_convert")
     return q, s, deq
+
+
+def weight_rotate2d(w: torch.Tensor, s_u: torch.Tensor, s_v: torch.Tensor, inverse: bool = False,
+                    shape: Optional[tuple] = None) -> torch.Tensor:
+    """Two-sided signed Hadamard rotation of a weight (the converter's
+    incoherence step, converters/quip_int8.py:523-551 / :1489-1506).
+
+    Forward: ``w`` [M, N] -> fp32 [M_pad, N_pad] = FHT_N(FHT_M(pad(w) s_u s_v^T)).
+    Inverse: ``w`` [M_pad, N_pad] -> fp32 ``shape`` (default [M_pad, N_pad]) =
+    slice(FHT_M(FHT_N(w)) s_u s_v^T).  Pads are ``len(s_u)``, ``len(s_v)``.
+    """
+    L.require_cuda(w)
+    assert w.dim() == 2, "weight must be 2-D"
+    w = w.contiguous()
+    Mp, Np = int(s_u.numel()), int(s_v.numel())
+    su = _sign(s_u, Mp, w.device)
+    sv = _sign(s_v, Np, w.device)
+    lib = L.load()
+    if not inverse:
+        M, N = w.shape
+        out = torch.empty((Mp, Np), dtype=torch.float32, device=w.device)
+        ws, nws = None, 0
+    else:
+        assert tuple(w.shape) == (Mp, Np), f"inverse rotation takes a [{Mp}, {Np}] matrix, got {tuple(w.shape)}"
+        M, N = shape if shape is not None else (Mp, Np)
+        out = torch.empty((M, N), dtype=torch.float32, device=w.device)
+        ws = torch.empty((Mp, Np), dtype=torch.float32, device=w.device)
+        nws = ws.numel() * 4
+    L.check(lib.qi8_weight_rotate2d(L.ptr(w), L.dtype_code(w.dtype), M, N, Mp, Np, L.ptr(su), L.ptr(sv),
+                                    int(bool(inverse)), L.ptr(out), L.ptr(ws), nws, L.stream_ptr(w.device)),
+            "qi8_weight_rotate2d")
+    return out
+
+
+def allgather_cols(y_local: torch.Tensor, nccl_comm: int, world: int,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """All-gather of column shards ``[T, n_loc]`` into ``[T, world * n_loc]``
+    over a caller-created NCCL communicator (``ncclComm_t`` as an integer)."""
+    L.require_cuda(y_local)
+    y_local = y_local.contiguous()
+    T, n_loc = y_local.shape
+    if out is None:
+        out = torch.empty((T, world * n_loc), dtype=y_local.dtype, device=y_local.device)
+    scratch = torch.empty((world, T, n_loc), dtype=y_local.dtype, device=y_local.device)
+    lib = L.load()
+    L.check(lib.qi8_allgather_cols(L.ptr(y_local), L.dtype_code(y_local.dtype), T, n_loc, L.ptr(out), out.stride(0),
+                                   ctypes.c_void_p(nccl_comm), L.ptr(scratch), scratch.numel() * scratch.element_size(),
+                                   L.stream_ptr(y_local.device)), "qi8_allgather_cols")
+    return out
 
 
 def requant_weight(w: torch.Tensor, requant: int = L.QI8_REQ_ROW, block: int = 128):

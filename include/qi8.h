@@ -204,6 +204,34 @@ QI8_API int qi8_quip_convert_noalloc(const void* w, int w_dtype, int64_t M, int6
                                      const float* s_v, int store_transformed, int requant, int block,
                                      int8_t* q_out, float* scale_out, float* dequant_out, void* stream);
 
+/* Two-sided signed Hadamard rotation of a weight, the incoherence step of
+   the QuIP converter on its own (converters/quip_int8.py:523-551 forward,
+   :1489-1506 inverse); each 1-D transform is normalized by float(1/sqrt(n)),
+   the M direction runs first on the way in and last on the way out.
+   inverse == 0: out [M_pad, N_pad] fp32 = FHT_N(FHT_M(pad(W) * s_u * s_v^T)),
+                 W [M, N] bf16/f16/f32 (zero padded); workspace unused.
+   inverse != 0: out [M, N] fp32 = slice(FHT_M(FHT_N(W)) * s_u * s_v^T),
+                 W [M_pad, N_pad] bf16/f16/f32; workspace >= M_pad*N_pad*4 bytes.
+   M_pad, N_pad: powers of two (rows <= 32768, 2 <= cols <= 32768);
+   s_u [M_pad], s_v [N_pad] are +-1 fp32.  out 16-byte aligned. */
+QI8_API int qi8_weight_rotate2d(const void* w, int w_dtype, int64_t M, int64_t N, int64_t M_pad, int64_t N_pad,
+                                const float* s_u, const float* s_v, int inverse, float* out, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* Column all-gather of a column-sharded linear (multi-GPU inference): rank
+   r holds Y[:, r*n_loc:(r+1)*n_loc] as a contiguous [rows, n_loc] tile
+   y_local; every rank receives Y [rows, G*n_loc] (row stride ld_out) in
+   y_out.  One ncclAllGather on `stream` into scratch (>= G*rows*n_loc
+   elements), then one re-layout kernel; G = ncclCommCount(nccl_comm).
+   nccl_comm is an ncclComm_t created by the caller; NCCL (libnccl.so.2) is
+   resolved on the first call, QI8_EUNSUPPORTED if it cannot be loaded.
+   dtype: bf16 / f16 / f32 / i32 / i8.  Replaces the gather half of the
+   column-parallel plan for the largest linears (the reference runs them on
+   one GPU only). */
+QI8_API int qi8_allgather_cols(const void* y_local, int dtype, int64_t rows, int64_t n_loc, void* y_out,
+                               int64_t ld_out, void* nccl_comm, void* scratch, int64_t scratch_bytes,
+                               void* stream);
+
 /* Original-space requantization of a weight W[M,N] (row stride ld_w) with the
    QuIP requant rule (converters/quip_int8.py:1614-1669): scale =
    max(amax/127, 1e-12), q = rint(w / scale) in [-127, 127]; QI8_REQ_ROW ->

@@ -392,6 +392,17 @@ def quip_unrotate_weight(q: np.ndarray, scale: np.ndarray, s_u: np.ndarray, s_v:
     return np.ascontiguousarray(wd[:M, :N])
 
 
+def quip_inverse_rotate(wr: np.ndarray, s_u: np.ndarray, s_v: np.ndarray, M: int, N: int) -> np.ndarray:
+    """Inverse incoherence rotation of a rotated-space matrix,
+    converters/quip_int8.py:1489-1506: ``FHT_N`` (rows) first, then ``FHT_M``
+    (columns), then ``* s_u * s_v``; slice ``[:M, :N]``."""
+    wd = fwht_rows(np.asarray(wr, np.float32), True)
+    wd = fwht_cols(wd, True)
+    wd = wd * np.asarray(s_u, np.float32)[:, None]
+    wd = wd * np.asarray(s_v, np.float32)[None, :]
+    return np.ascontiguousarray(wd[:M, :N])
+
+
 def quip_requant(w: np.ndarray, scheme: str = "tensor", per_row: bool = True,
                  block_size: int = 128) -> Tuple[np.ndarray, np.ndarray]:
     """Original-space requantization, converters/quip_int8.py:1614-1669.

@@ -350,6 +350,32 @@ def test_quip_convert_random_vs_oracle(M, N):
     assert np.array_equal(np_(q), qr) and np.array_equal(np_(s).reshape(sr.shape), sr)
 
 
+@pytest.mark.parametrize("M,N", [(128, 256), (96, 192), (1000, 700), (4096, 512), (300, 16384)])
+def test_weight_rotate2d_vs_oracle(M, N):
+    # the converter's incoherence rotation on its own, forward and inverse
+    r = rng(7 * M + N)
+    w = (r.standard_normal((M, N)) * 0.02).astype(np.float32)
+    wb = torch.from_numpy(w).to(torch.bfloat16)
+    Mp, Np = O.next_power_of_two(M), O.next_power_of_two(N)
+    su = (r.integers(0, 2, Mp) * 2 - 1).astype(np.float32)
+    sv = (r.integers(0, 2, Np) * 2 - 1).astype(np.float32)
+    wr = ops.weight_rotate2d(wb.to(dev()), cu(su), cu(sv))
+    ref = O.quip_rotate_weight(wb.float().numpy(), su, sv)
+    assert np.array_equal(np_(wr), ref)
+    back = ops.weight_rotate2d(wr, cu(su), cu(sv), inverse=True, shape=(M, N))
+    assert np.array_equal(np_(back), O.quip_inverse_rotate(ref, su, sv, M, N))
+    # orthogonal: the round trip returns the weight up to fp32 rounding
+    assert np.max(np.abs(np_(back) - wb.float().numpy())) < 1e-6
+
+
+def test_weight_rotate2d_rejects_bad_sizes():
+    w = torch.zeros(8, 8, device=dev())
+    with pytest.raises(AssertionError):
+        ops.weight_rotate2d(w, torch.ones(12, device=dev()), torch.ones(8, device=dev()))  # 12 not a power of 2
+    with pytest.raises(AssertionError):
+        ops.weight_rotate2d(w, torch.ones(8, device=dev()), torch.ones(16, device=dev()), inverse=True)
+
+
 # -------------------------------------------------- rotated W8A8 linear
 def test_quip_w8a8_linear_vs_reference_fp32(golden):
     g = golden("quip_matmul.npz")

@@ -201,6 +201,28 @@ def test_column_sharded_linear_single_rank_equals_full(kind):
     assert torch.equal(torch.cat(halves, dim=1), y)
 
 
+@pytest.mark.parametrize("kind", ["row", "block"])
+def test_column_sharded_linear_overlapped_chunks(kind):
+    # the chunked GEMM + asynchronous all-gather path over a one-rank NCCL group
+    import torch.distributed as dist
+    r = np.random.default_rng(6)
+    x = torch.from_numpy(r.standard_normal((48, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
+    w = (torch.from_numpy(r.standard_normal((512, 512)).astype(np.float32)) * 0.02).cuda()
+    bias = torch.from_numpy(r.standard_normal(512).astype(np.float32)).to(torch.bfloat16).cuda()
+    q, s = ops.requant_weight(w, L.QI8_REQ_ROW if kind == "row" else L.QI8_REQ_BLOCK)
+    full = sharding.ColumnShardedW8A8Linear(q, s, bias, rank=0, world=1)(x)
+    dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
+                            device_id=torch.device("cuda", 0))
+    try:
+        lin = sharding.ColumnShardedW8A8Linear(q, s, bias, rank=0, world=1, chunks=4)
+        assert lin.chunks == 4
+        y = lin(x)
+        torch.cuda.synchronize()
+    finally:
+        dist.destroy_process_group()
+    assert torch.equal(y, full)
+
+
 def test_conversion_partition_single_gpu():
     shapes = [(384, 256), (256, 640), (128, 128)]
     names = [f"t{i}" for i in range(3)]

@@ -171,3 +171,12 @@ def test_lpt_partition_balanced():
     assert sorted(i for p in parts for i in p) == list(range(10))
     loads = [sum(costs[i] for i in p) for p in parts]
     assert max(loads) - min(loads) <= 2
+
+
+def test_oracle_rotation_round_trip():
+    r = np.random.default_rng(5)
+    w = (r.standard_normal((100, 60)) * 0.02).astype(np.float32)
+    su = (r.integers(0, 2, 128) * 2 - 1).astype(np.float32)
+    sv = (r.integers(0, 2, 64) * 2 - 1).astype(np.float32)
+    back = O.quip_inverse_rotate(O.quip_rotate_weight(w, su, sv), su, sv, 100, 60)
+    assert np.max(np.abs(back - w)) < 1e-6

@@ -39,7 +39,9 @@ def _worker_plan(rank, world, port, q):
         T = 3
         y_local = torch.arange(T * 4, dtype=torch.float32).reshape(T, 4) + 100 * rank
         y = sharding.gather_columns(y_local, world)
-        q.put((rank, everyone, y))
+        # overlapped chunked gather: chunk k of rank r = columns k*2 .. k*2+1 of its shard
+        y_chunked = sharding.gather_columns_overlapped(lambda k: y_local[:, 2 * k:2 * k + 2], 2, world)
+        q.put((rank, everyone, y, y_chunked))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, "error", repr(e)))
@@ -104,6 +106,7 @@ def test_gloo_plan_agreement_and_column_gather(world):
     expect = torch.cat([torch.arange(12, dtype=torch.float32).reshape(3, 4) + 100 * r for r in range(world)], dim=1)
     for r in range(world):
         assert torch.equal(res[r][1], expect)
+        assert torch.equal(res[r][2], expect)
 
 
 def test_gloo_rank_failure_is_reported_not_hung():
