@@ -26,10 +26,11 @@
 //   * block-scaled epilogue (per-128-K-block scales): one unit per K block;
 //     the epilogue promotes each block's int32 partial to fp32 and
 //     accumulates acc += p * sa * sb in registers (int8_gemm semantics,
-//     comfy/int8_kernels.py:468-480).  The int32 -> fp32 conversion uses the
-//     exact 1.5*2^23 bias trick (|p| <= 128*128*128 < 2^22) so it costs one
-//     integer add and half a packed fp32 add instead of a low-throughput
-//     I2F; TMEM loads of the next 32 columns are in flight during the math.
+//     comfy/int8_kernels.py:468-480): one I2F and half a packed FFMA per
+//     partial (the sm_100 I2F is cheaper than the exact 1.5*2^23 integer-add
+//     trick, which costs an INT add plus half a packed FADD, by 15-18 % in
+//     the whole kernel); TMEM loads of the next 32 columns are in flight
+//     during the math.
 //
 // Every mbarrier wait is bounded (globaltimer); on expiry the waiting role
 // sets a bit in the device status word and an abort flag in shared memory,
@@ -69,11 +70,6 @@ constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) +
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;  // 0.2 s when cleaning up
 
-// Exact int32 -> fp32 of a K-block partial p (|p| <= 128*128*128 < 2^22):
-// the bits of 0x4B400000 + p are the fp32 value 1.5*2^23 + p, so one integer
-// add and one fp32 subtract convert it (instead of a low-throughput I2F).
-constexpr uint32_t MAGIC_BITS = 0x4B400000u;
-constexpr float MAGIC_F = 12582912.0f;
 
 // instruction descriptor: D s32, A/B signed int8, both K-major, N=256, M=128
 constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -661,10 +657,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int col = c * 32 + 2 * j;
-                // exact int32 -> fp32 (|p| < 2^22): bits(0x4B400000 + p) = 1.5*2^23 + p
-                float2 f = make_float2(__uint_as_float(rb[c & 1][2 * j] + MAGIC_BITS),
-                                       __uint_as_float(rb[c & 1][2 * j + 1] + MAGIC_BITS));
-                f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
+                // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
+                const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                             __int2float_rn((int)rb[c & 1][2 * j + 1]));
                 float2 sc = sk2;
                 if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
                 acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
@@ -1056,10 +1051,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int col = c * 32 + 2 * j;
-                // exact int32 -> fp32 (|p| < 2^22): bits(0x4B400000 + p) = 1.5*2^23 + p
-                float2 f = make_float2(__uint_as_float(rb[c & 1][2 * j] + MAGIC_BITS),
-                                       __uint_as_float(rb[c & 1][2 * j + 1] + MAGIC_BITS));
-                f = __fadd2_rn(f, make_float2(-MAGIC_F, -MAGIC_F));
+                // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
+                const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                             __int2float_rn((int)rb[c & 1][2 * j + 1]));
                 float2 sc = sk2;
                 if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
                 acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
