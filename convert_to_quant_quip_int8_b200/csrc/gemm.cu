@@ -63,10 +63,11 @@ constexpr int EPI_REGS = 240;
 constexpr int CTRL_REGS = 24;
 static_assert(256 * EPI_REGS + 128 * CTRL_REGS == THREADS * LAUNCH_REGS, "register split must balance");
 constexpr uint32_t TMEM_COLS = 512;
-// column scales, bias, per-kb scales (fp32 x 128 per warp each) + a 32x16 bf16 transpose tile per warp
-constexpr int STAGE_SCRATCH_BYTES = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 16 * 32 * 2;
+// column scales, bias, per-kb scales (fp32 x 128 per warp each) + two 32x16 bf16 transpose tiles per warp
+constexpr int STAGE_SCRATCH_BYTES = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 2 * 16 * 32 * 2;
 constexpr int NUM_BARS = 2 * STAGES + 8 + 1;  // full, empty, tfull[2][2], tempty[2][2], drain
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES + NUM_BARS * 8 + 16;
+static_assert(SMEM_BYTES <= 232448, "shared memory");
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per wait
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;  // 0.2 s when cleaning up
 
@@ -337,17 +338,34 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
   constexpr int RUN = WC / 2;
   const bool row_ok = rr < R;
   if constexpr (SWAP) {
-    __nv_bfloat16* tb = sxp + warp * (16 * 32);
+    // two 16x32 bf16 transpose tiles per warp, used alternately, so one
+    // __syncwarp per chunk orders the writes before the transposed reads and
+    // the reads of chunk c before the writes of chunk c + 2
+    __nv_bfloat16* tbw = sxp + warp * (2 * 16 * 32);
+    const bool unit_row = p.b_kind == QI8_S_ROW_KBLOCK;  // frow == 1 exactly
+    const bool has_bias = p.bias != nullptr;
 #pragma unroll
     for (int c = 0; c < WC / 16; ++c) {
       const int col0 = c * 16 < RUN ? cc0 + c * 16 : cc1 + c * 16 - RUN;
-      if (col0 >= C) continue;  // warp-uniform
+      if (col0 >= C) {  // warp-uniform; keeps one __syncwarp per chunk
+        __syncwarp();
+        continue;
+      }
       if (p.out_dtype == QI8_BF16) {
+        __nv_bfloat16* tb = tbw + (c & 1) * (16 * 32);
+        float cs[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = reinterpret_cast<const float4*>(my_col + c * 16)[q];
+          cs[4 * q] = v.x; cs[4 * q + 1] = v.y; cs[4 * q + 2] = v.z; cs[4 * q + 3] = v.w;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int col = c * 16 + j;
           const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
-          float y = __fadd_rn(__fmul_rn(__fmul_rn(a, my_col[col]), frow), brow);
+          float y = __fmul_rn(a, cs[j]);
+          if (!unit_row) y = __fmul_rn(y, frow);
+          if (has_bias) y = __fadd_rn(y, brow);
           if (GELU) y = act_gelu(y, p.out_dtype);
           tb[j * 32 + lane] = __float2bfloat16_rn(y);
         }
@@ -361,7 +379,6 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
           dst[0] = src[0];
           dst[1] = src[1];
         }
-        __syncwarp();
       } else if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -383,12 +400,18 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
     for (int g = 0; g < WC / 8; ++g) {
       const int n0 = g * 8 < RUN ? cc0 + g * 8 : cc1 + g * 8 - RUN;
       if (n0 >= C) continue;
+      const float4 c0 = reinterpret_cast<const float4*>(my_col + g * 8)[0];
+      const float4 c1 = reinterpret_cast<const float4*>(my_col + g * 8)[1];
+      const float4 b0 = reinterpret_cast<const float4*>(my_bias + g * 8)[0];
+      const float4 b1 = reinterpret_cast<const float4*>(my_bias + g * 8)[1];
+      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
       float y[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int col = g * 8 + j;
         const float a = (j & 1) ? acc[col >> 1].y : acc[col >> 1].x;
-        y[j] = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), my_col[col]), my_bias[col]);
+        y[j] = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), cs[j]), bs[j]);
         if (GELU) y[j] = act_gelu(y[j], p.out_dtype);
       }
       store_row8(p, rr, n0, y);
@@ -413,7 +436,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   float* scol = reinterpret_cast<float*>(sb + STAGES * (A_BYTES + B_BYTES));  // [8 warps][128] column scales
   float* sbias = scol + NUM_EPI_WARPS * 128;                                   // [8 warps][128] bias
   float* skb = sbias + NUM_EPI_WARPS * 128;                                    // [8 warps][128] per-kb scales
-  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][16][32] transpose
+  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][2][16][32] transpose
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + STAGES * (A_BYTES + B_BYTES) + STAGE_SCRATCH_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -765,7 +788,7 @@ constexpr int P_BUFS = 2;  // TMEM accumulator buffers of 256 columns
 constexpr uint32_t IDESC_P256 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                                 ((uint32_t)(256 >> 4) << 24);
 constexpr int P_NUM_BARS = 2 * P_STAGES + 2 * P_BUFS + 1;  // full, empty, tfull, tempty, drain
-constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 16 * 32 * 2;
+constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 2 * 16 * 32 * 2;
 constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + P_SCRATCH + P_NUM_BARS * 8 + 16;
 static_assert(P_SMEM <= 232448, "shared memory");
 
@@ -829,7 +852,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   float* scol = reinterpret_cast<float*>(sb + P_STAGES * P_STAGE_BYTES);  // [8 warps][128] column scales
   float* sbias = scol + NUM_EPI_WARPS * 128;                              // [8 warps][128] bias
   float* skb = sbias + NUM_EPI_WARPS * 128;                               // [8 warps][128] per-kb scales
-  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][16][32]
+  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][2][16][32]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + P_STAGES * P_STAGE_BYTES + P_SCRATCH);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P_NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
