@@ -300,8 +300,223 @@ __global__ void __launch_bounds__(RotCfg<L>::THREADS) rotate_rows_kernel(RotArgs
   }
 }
 
+// ============================================ phased row FWHT (2^9..2^14)
+// One row of n = 2^L fp32 values per CTA of P = n/16 threads (persistent
+// over rows).  Each thread holds 16 elements whose indices differ only in a
+// 4-bit window of the index; the window moves up by 4 bits per phase
+// (0, 4, 8, ..., and L-4 last), and the data moves between phases through
+// shared memory.  Stages run in ascending bit (stride) order, so results are
+// bit-identical to the single-row kernel above.  The shared-memory layout
+// swaps 16-byte chunks (chunk ^= row bits 5..7 ^ index bit 8 << 2), which
+// makes every phase's accesses bank-conflict free, including the 128-bit
+// writes of the first phase.  Per-token quantization stores 16 contiguous
+// bytes per thread after a byte-wide transpose.
+namespace rot2 {
+
+// The swizzle is linear over XOR, so for an index base ^ off (disjoint bits)
+// phys = swz(base) ^ swz(off): a per-thread base and a compile-time offset.
+__host__ __device__ constexpr int swz(int i) {
+  return i ^ (((i >> 5) & 7) << 2) ^ (((i >> 8) & 1) << 4);
+}
+// index of element e (window bits) of thread t for the window starting at
+// bit w is wbase(t, w) | (e << w)
+__device__ __forceinline__ int wbase(int t, int w) { return (t & ((1 << w) - 1)) | ((t >> w) << (w + 4)); }
+template <int L>
+__host__ __device__ constexpr int nwin() { return (L + 3) / 4; }
+template <int L>
+__host__ __device__ constexpr int wstart(int k) { return k < nwin<L>() - 1 ? 4 * k : L - 4; }
+
+// butterflies of index bits [4k, min(4k + 4, L)) on the window of phase k;
+// strides >= 2 run as packed fp32 pairs (sum, and difference as
+// fma(hi, -1, lo): both single-rounded, identical to the scalar ops)
+template <int L, int K>
+__device__ __forceinline__ void stages(float (&v)[16]) {
+  constexpr int w = wstart<L>(K);
+  constexpr int hi = (4 * K + 4 < L) ? 4 * K + 4 : L;
+#pragma unroll
+  for (int bit = 4 * K; bit < hi; ++bit) {
+    const int s = 1 << (bit - w);
+    if (s == 1) {
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        const float lo = v[e], hi_v = v[e + 1];
+        v[e] = lo + hi_v;
+        v[e + 1] = lo - hi_v;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        if (!(e & s)) {
+          const float2 lo = make_float2(v[e], v[e + 1]);
+          const float2 hv = make_float2(v[e + s], v[e + s + 1]);
+          const float2 sm = __fadd2_rn(lo, hv);
+          const float2 df = __ffma2_rn(hv, make_float2(-1.0f, -1.0f), lo);
+          v[e] = sm.x;
+          v[e + 1] = sm.y;
+          v[e + s] = df.x;
+          v[e + s + 1] = df.y;
+        }
+      }
+    }
+  }
+}
+
+template <int L, int K>
+__device__ __forceinline__ void phase(float (&v)[16], float* buf, int t) {
+  if constexpr (K < nwin<L>()) {
+    constexpr int wp = wstart<L>(K - 1), w = wstart<L>(K);
+    if constexpr (K == 1) {
+      const int sb = swz(t * 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4*>(buf + (sb ^ swz(4 * j))) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      const int sb = swz(wbase(t, wp));
+#pragma unroll
+      for (int e = 0; e < 16; ++e) buf[sb ^ swz(e << wp)] = v[e];
+    }
+    __syncthreads();
+    const int sb = swz(wbase(t, w));
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = buf[sb ^ swz(e << w)];
+    stages<L, K>(v);
+    phase<L, K + 1>(v, buf, t);
+  }
+}
+
+// two row buffers, used by alternate rows (no barrier between rows)
+template <int L>
+constexpr int smem_bytes() { return 2 * (1 << L) * 4; }
+
+template <int L, typename T, int OUT>
+__global__ void __launch_bounds__(1 << (L - 4), 1024 >> (L - 4)) rot2_kernel(RotArgs a, int64_t rows) {
+  constexpr int N = 1 << L, P = N / 16, NW = nwin<L>(), WL = wstart<L>(NW - 1);
+  extern __shared__ float4 dyn_smem[];
+  float* bufs = reinterpret_cast<float*>(dyn_smem);
+  __shared__ float red[2][32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int c0 = t * 16;
+  // the next row's 16 raw elements are loaded while this row is transformed
+  // (rows whose width is a multiple of 16 and whose pointers allow vectors)
+  constexpr int NR = 16 * (int)sizeof(T) / 16;
+  const bool pre = a.vec != 0 && (a.n_in & 15) == 0;
+  const bool mine = c0 < a.n_in;
+  uint4 raw[NR];
+  auto fetch = [&](int64_t r) {
+#pragma unroll
+    for (int k = 0; k < NR; ++k) raw[k] = make_uint4(0, 0, 0, 0);
+    if (r < rows && mine) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + r * a.ld_x + c0);
+#pragma unroll
+      for (int k = 0; k < NR; ++k) raw[k] = __ldg(p + k);
+    }
+  };
+  if (pre) fetch(blockIdx.x);
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    // a row's first write to its buffer follows the first barrier of the
+    // previous row, which every thread passes only after finishing the row
+    // before it -- the last reader of this buffer
+    float* buf = bufs + (it & 1) * N;
+    const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
+    float v[16];
+    if (pre) {
+      const T* tv = reinterpret_cast<const T*>(raw);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = to_f32<T>(tv[e]);
+      fetch(row + gridDim.x);
+    } else {
+      load_run<T, 16>(xr, c0, a.n_in, a.vec != 0, v);
+    }
+    if (a.pre_sign) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.pre_sign + c0) + q);
+        v[4 * q] = __fmul_rn(v[4 * q], s4.x);
+        v[4 * q + 1] = __fmul_rn(v[4 * q + 1], s4.y);
+        v[4 * q + 2] = __fmul_rn(v[4 * q + 2], s4.z);
+        v[4 * q + 3] = __fmul_rn(v[4 * q + 3], s4.w);
+      }
+    }
+    stages<L, 0>(v);
+    phase<L, 1>(v, buf, t);
+    if (a.do_norm) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], a.norm);
+    }
+    if constexpr (OUT == RO_Q_TOKEN) {
+      float m = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+      m = warp_max(m);
+      if (lane == 0) red[it & 1][warp] = m;
+      __syncthreads();
+      float amax = red[it & 1][0];
+#pragma unroll 1
+      for (int w = 1; w < P / 32; ++w) amax = fmaxf(amax, red[it & 1][w]);
+      const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+      const float rcp = __frcp_rn(s);
+      // one byte per element in the last window's mapping: a warp writes 32
+      // consecutive bytes per element index
+      int8_t* qrow = a.q + row * N + wbase(t, WL);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        // rint(fl(v * rcp)) in [-127, 127]: low byte of fl(fl(v * rcp) + 1.5 * 2^23)
+        const float r = __fadd_rn(__fmul_rn(v[e], rcp), 12582912.0f);
+        qrow[e << WL] = (int8_t)(__float_as_uint(r) & 0xFF);
+      }
+      if (t == 0) a.scale[row] = s;
+    } else if constexpr (OUT == RO_F32) {
+      float* dst = a.f_out + row * N;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = wbase(t, WL) + (e << WL);
+        float y = v[e];
+        if (a.post_sign) y = __fmul_rn(y, __ldg(a.post_sign + i));
+        dst[i] = y;
+      }
+    } else {  // RO_UNROT
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int i = wbase(t, WL) + (e << WL);
+        if (i < a.n_out) {
+          float y = v[e];
+          if (a.post_sign) y = __fmul_rn(y, __ldg(a.post_sign + i));
+          if (a.bias) y = __fadd_rn(y, load_as_f32(a.bias, a.bias_dtype, i));
+          store_from_f32(a.out, a.out_dtype, row * a.ld_out + i, y);
+        }
+      }
+    }
+  }
+}
+
+template <int L, typename T, int OUT>
+int launch(const RotArgs& a, int64_t rows, cudaStream_t st) {
+  constexpr int P = 1 << (L - 4);
+  constexpr int SMEM = smem_bytes<L>();
+  auto kern = rot2_kernel<L, T, OUT>;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    if (SMEM > 48 * 1024) QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, P, SMEM) != cudaSuccess || b < 1) b = 1;
+    per_sm = b;
+  }
+  const int64_t cap = (int64_t)(sm_count() > 0 ? sm_count() : 148) * per_sm;
+  const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+  kern<<<grid, P, SMEM, st>>>(a, rows);
+  return check_cuda(cudaGetLastError(), "rot2_kernel launch");
+}
+
+}  // namespace rot2
+
 template <int L, typename T, int OUT>
 int launch_rotate_L(const RotArgs& a, int64_t rows, cudaStream_t st) {
+  // rows of 2^9 .. 2^14: the phased kernel (vector loads of the pre-signs
+  // need them 16-byte aligned); block-128 quantization stays below
+  if constexpr (L >= 9 && L <= 14 && OUT != RO_Q_BLOCK) {
+    if (!a.pre_sign || (reinterpret_cast<uintptr_t>(a.pre_sign) & 15) == 0) return rot2::launch<L, T, OUT>(a, rows, st);
+  }
   using C = RotCfg<L>;
   auto kern = rotate_rows_kernel<L, T, OUT>;
   if (C::SMEM > 48 * 1024) {
