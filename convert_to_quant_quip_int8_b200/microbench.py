@@ -1,0 +1,121 @@
+"""Kernel micro-benchmarks of the QuIP W8A8 path (one GPU).
+
+    python -m convert_to_quant_quip_int8_b200.microbench rotate   # K1 rotate+quant, K3 unrotate
+    python -m convert_to_quant_quip_int8_b200.microbench quant    # K1 per-token quant (+ fused GELU)
+    python -m convert_to_quant_quip_int8_b200.microbench gemm     # K2 block-scaled / per-row GEMM
+    python -m convert_to_quant_quip_int8_b200.microbench convert  # K4 QuIP conversion
+
+Each case is timed with CUDA events around one launch, median of ``--iters``
+launches, with a 256 MB buffer rewritten between launches so every launch
+reads its inputs from HBM.  Prints one JSON object: case -> [us, GB/s or
+TOPS].  ``--profile`` runs every case ``--iters`` times without timing (the
+form to run under ncu).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib as L
+from . import ops
+
+
+def _timer(flush: torch.Tensor, iters: int, profile: bool):
+    def run(fn):
+        for _ in range(2):
+            fn()
+        if profile:
+            for _ in range(iters):
+                fn()
+            torch.cuda.synchronize()
+            return float("nan")
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        ts.sort()
+        return ts[len(ts) // 2]
+    return run
+
+
+def _signs(n: int, dev) -> torch.Tensor:
+    g = torch.Generator(device="cpu").manual_seed(n)
+    return (torch.randint(0, 2, (n,), generator=g) * 2 - 1).float().to(dev)
+
+
+def rotate_cases(run, dev):
+    res = {}
+    for T, n, npad in [(512, 4096, 4096), (4096, 3072, 4096), (4608, 15360, 16384)]:
+        x = torch.randn(T, n, device=dev).to(torch.bfloat16)
+        sv = _signs(npad, dev)
+        us = run(lambda: ops.rotate_quant_rows(x, sv, npad))
+        res[f"k1_rotate_quant_{T}x{n}->{npad}"] = [us, (T * n * 2 + T * npad + T * 4) / us / 1e3]
+        y = torch.randn(T, npad, device=dev)
+        us = run(lambda: ops.unrotate_rows(y, sv, n, None, torch.bfloat16))
+        res[f"k3_unrotate_{T}x{npad}->{n}"] = [us, (T * npad * 4 + T * n * 2) / us / 1e3]
+    return res
+
+
+def quant_cases(run, dev):
+    res = {}
+    for n, mode, name in [(3072, L.QI8_Q_TOKEN, "token"), (12288, L.QI8_Q_TOKEN, "token"),
+                          (12288, L.QI8_Q_TOKEN | L.QI8_Q_GELU, "gelu_token")]:
+        x = torch.randn(4096, n, device=dev).to(torch.bfloat16)
+        us = run(lambda: ops.quant_rows(x, mode))
+        res[f"k1_{name}_4096x{n}"] = [us, 4096 * (n * 3 + 4) / us / 1e3]
+    return res
+
+
+def gemm_cases(run, dev):
+    res = {}
+    for M, N, K in [(4096, 12288, 3072), (4096, 3072, 12288)]:
+        a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=dev)
+        b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=dev)
+        sa = torch.rand(M, 1, device=dev) * 0.01
+        sbk = torch.rand(N, K // 128, device=dev) * 0.01
+        sb = torch.rand(N, 1, device=dev) * 0.01
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, sbk, L.QI8_S_ROW_KBLOCK, None, torch.bfloat16, out=out))
+        res[f"k2_block_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+        us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, sb, L.QI8_S_ROW, None, torch.bfloat16, out=out))
+        res[f"k2_row_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+    return res
+
+
+def convert_cases(run, dev):
+    res = {}
+    for M, N in [(3072, 3072), (12288, 3072), (3072, 12288)]:
+        w = (torch.randn(M, N, device=dev) * 0.02).to(torch.bfloat16)
+        Mp, Np = 1 << (M - 1).bit_length(), 1 << (N - 1).bit_length()
+        su, sv = _signs(Mp, dev), _signs(Np, dev)
+        ws = torch.empty(ops.quip_workspace_bytes(M, N), dtype=torch.uint8, device=dev)
+        us = run(lambda: ops.quip_convert(w, su, sv, requant=L.QI8_REQ_BLOCK, want_dequant=False, workspace=ws))
+        res[f"k4_quip_convert_block_{M}x{N}"] = [us, M * N * 2 / us / 1e3]
+    return res
+
+
+CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "convert": convert_cases}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--profile", action="store_true")
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = CASES[args.case](_timer(flush, args.iters, args.profile), dev)
+    print(json.dumps({k: [round(v[0], 2), round(v[1], 1)] for k, v in res.items()}))
+
+
+if __name__ == "__main__":
+    main()
