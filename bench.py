@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--impl", default="qi8", choices=["qi8", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=512, help="token sample of the CPU baseline step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="dit_mlp", choices=["dit_mlp", "quip_linear", "conversion"],
+                    help="dit_mlp: the headline DiT MLP pair; quip_linear: one rotated W8A8 linear "
+                         "(K1 rotate -> K2 -> K3); conversion: the 304-tensor QuIP conversion sweep")
     return ap.parse_args()
 
 
@@ -218,10 +221,132 @@ def build_model(device):
     return wl, x, (q1, s1.reshape(q1.shape[0], -1).contiguous()), (q2, s2.reshape(q2.shape[0], -1).contiguous())
 
 
+def timed_region(step, steps, world, device):
+    """Runs ``steps`` calls of ``step`` between barriers and device syncs;
+    returns the max over ranks of the CUDA-event time (ms) and the clocks."""
+    stream = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockProbe(device.index if device.index is not None else 0) as probe:
+        barrier(world)
+        torch.cuda.synchronize(device)
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+    return max_over_ranks(t0.elapsed_time(t1), world, device), probe.summary()
+
+
+def main_quip_linear(args):
+    """Config 1: one QuIP W8A8 linear in transformed storage (tensorwise
+    scale): x [512, 4096] -> K1 (signs + FWHT + per-token int8) -> K2 (int8
+    GEMM, fp32 out) -> K3 (FWHT + signs + bias -> bf16)."""
+    from convert_to_quant_quip_int8_b200 import _lib as L
+    from convert_to_quant_quip_int8_b200 import ops
+    from convert_to_quant_quip_int8_b200.workloads import SingleQuipLinear
+
+    rank, world, local = dist_init(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = SingleQuipLinear()
+    su, sv = wl.signs()
+    q, s, _ = ops.quip_convert(wl.weight().to(device), su, sv, store_transformed=True, want_dequant=False)
+    su_d, sv_d = su.to(device), sv.to(device)
+    x = wl.activations().to(device)
+    bias = wl.bias().to(device)
+    T, D = wl.tokens, wl.dim
+
+    def step():
+        xq, xs = ops.rotate_quant_rows(x, sv_d, D)
+        y_had = ops.gemm_i8(xq, q, xs, L.QI8_S_ROW, s, L.QI8_S_ROW, None, torch.float32)
+        return ops.unrotate_rows(y_had, su_d, D, bias, torch.bfloat16)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    ms, clocks = timed_region(step, args.steps, world, device)
+    ops.device_status()
+    ops_step = 2 * T * D * D
+    value = world * ops_step * args.steps / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "QuIP W8A8 rotated linear TOPS (transformed storage, tensorwise scale)",
+            "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (fp32 epilogue, bf16 out)",
+            "data": "synthetic (seeded: W N(0,0.02), x N(0,1) with 40 outlier channels x20)",
+            "config": {"workload": "quip_linear: x[512,4096] bf16, W'[4096,4096] int8 + scalar scale, signs 4096+4096",
+                       "tokens": T, "dim": D, "l2": "inputs fit in L2 (~25 MB): L2-resident steady state"},
+            "gpu_launches": 3 * args.steps, "clocks": clocks}), flush=True)
+    _finish(world)
+
+
+def main_conversion(args):
+    """Config 5: the QuIP conversion sweep (304 tensors, 12.9 B params).
+    Tensors are partitioned over ranks by longest-processing-time on the
+    padded size (no collective); each rank's bf16 weights are resident in
+    HBM before the timed region; one step converts all of this rank's
+    tensors (two-sided FWHT, rotated RTN, inverse, block-128 requant)."""
+    from convert_to_quant_quip_int8_b200 import _lib as L
+    from convert_to_quant_quip_int8_b200 import ops, sharding
+    from convert_to_quant_quip_int8_b200.workloads import conversion_sweep_tensors
+
+    rank, world, local = dist_init(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    tensors = conversion_sweep_tensors()
+    shapes = [(m, n) for _, m, n in tensors]
+    mine = sharding.plan_partition(shapes, world)[rank]
+    gen = torch.Generator(device=device)
+    weights, signs = [], []
+    for i in mine:
+        m, n = shapes[i]
+        gen.manual_seed(50 + i)
+        weights.append((torch.randn(m, n, generator=gen, device=device) * 0.02).to(torch.bfloat16))
+        mp, np_ = 1 << (m - 1).bit_length(), 1 << (n - 1).bit_length()
+        gen.manual_seed(1000 + i)
+        signs.append(((torch.randint(0, 2, (mp,), generator=gen, device=device) * 2 - 1).float(),
+                      (torch.randint(0, 2, (np_,), generator=gen, device=device) * 2 - 1).float()))
+    max_ws = max(ops.quip_workspace_bytes(*shapes[i]) for i in mine)
+    ws = torch.empty(max_ws, dtype=torch.uint8, device=device)
+    max_mn = max(shapes[i][0] * shapes[i][1] for i in mine)
+    qbuf = torch.empty(max_mn, dtype=torch.int8, device=device)
+
+    def step():
+        for w, (su, sv) in zip(weights, signs):
+            ops.quip_convert(w, su, sv, requant=L.QI8_REQ_BLOCK, want_dequant=False, workspace=ws)
+        return qbuf
+
+    step()
+    torch.cuda.synchronize(device)
+    steps = max(1, args.steps)
+    ms, clocks = timed_region(step, steps, world, device)
+    ops.device_status()
+    params = sum(shapes[i][0] * shapes[i][1] for i in range(len(shapes)))
+    value = len(shapes) * steps / (ms / 1e3)  # tensors/s of the whole job
+    if rank == 0:
+        print(json.dumps({
+            "metric": "QuIP conversion sweep tensors/s (304 tensors, 12.9 B params)",
+            "value": round(value, 2), "unit": "tensors/s", "n_gpus": world, "steps": steps, "warmup": 1,
+            "ms_per_step": round(ms / steps, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32 transform, int8 out",
+            "weight_gb_per_s": round(params * 2 * steps / (ms / 1e3) / 1e9, 1),
+            "data": "synthetic (seeded N(0,0.02) bf16 weights resident in HBM)",
+            "config": {"workload": "conversion_sweep: 304 tensors, LPT partition by padded size, block-128 requant",
+                       "params": params, "parallelism": f"tensor-partitioned x{world}"},
+            "clocks": clocks}), flush=True)
+    _finish(world)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return main_reference(args)
+    if args.workload == "quip_linear":
+        return main_quip_linear(args)
+    if args.workload == "conversion":
+        return main_conversion(args)
     from convert_to_quant_quip_int8_b200 import _lib as L
     from convert_to_quant_quip_int8_b200 import ops
     from convert_to_quant_quip_int8_b200.comfy.quant_ops import QuantizedTensor

@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
   const int64_t lo = blockIdx.y % lo_count, hi = blockIdx.y / lo_count;
   const int64_t hi_base = lo + (hi << (a.b0 + a.rbits));
 
+  // unrolled so that a warp keeps several row loads in flight
+#pragma unroll 8
   for (int k = warp; k < R; k += NW) {
     const int64_t i = hi_base + ((int64_t)k << a.b0);
     float v = 0.0f;
@@ -74,6 +76,7 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
   }
   __syncthreads();
   for (int h = 1; h < R; h <<= 1) {
+#pragma unroll 4
     for (int p = warp; p < (R >> 1); p += NW) {
       const int k = ((p / h) * 2 * h) + (p % h);
       const float lo_v = tile[k * COL_STRIP + lane];
@@ -83,6 +86,7 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
     }
     __syncthreads();
   }
+#pragma unroll 8
   for (int k = warp; k < R; k += NW) {
     const int64_t i = hi_base + ((int64_t)k << a.b0);
     float v = tile[k * COL_STRIP + lane];

@@ -712,8 +712,13 @@ __global__ void __launch_bounds__(256, 3) token_rows_kernel(QArgs a, int rows, i
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if constexpr (GELU) {
+            // gelu_erf on a pair: (0.5 x) * (1 + erf(x / sqrt 2)), the same
+            // separately rounded products and sum as the scalar form
             const float2 f = Pack<T>::f2(w[j]);
-            w[j] = Pack<T>::from_f2(gelu_erf(f.x), gelu_erf(f.y));
+            const float2 tt = __fmul2_rn(f, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
+            const float2 e = make_float2(erff(tt.x), erff(tt.y));
+            const float2 g = __fmul2_rn(__fmul2_rn(f, make_float2(0.5f, 0.5f)), __fadd2_rn(make_float2(1.0f, 1.0f), e));
+            w[j] = Pack<T>::from_f2(g.x, g.y);
           }
           m = Pack<T>::absmax2(m, w[j]);
         }

@@ -138,6 +138,16 @@ def test_quant_rows_gelu_fused(n):
     assert np.allclose(np_(s), sr, rtol=1e-2)
 
 
+@pytest.mark.parametrize("n", [3072, 12288])
+def test_quant_rows_gelu_equals_torch_gelu_then_quant(n):
+    # the fused GELU reproduces torch's bf16 F.gelu on the GPU bit for bit
+    r = rng(n + 7)
+    h = torch.from_numpy((r.standard_normal((257, n)) * 3).astype(np.float32)).to(torch.bfloat16).to(dev())
+    q, s = ops.quant_rows(h, L.QI8_Q_TOKEN | L.QI8_Q_GELU)
+    q2, s2 = ops.quant_rows(torch.nn.functional.gelu(h), L.QI8_Q_TOKEN)
+    assert torch.equal(q, q2) and torch.equal(s, s2)
+
+
 def test_quant_rows_block_golden(golden):
     g = golden("triton_quant.npz")
     q, s = ops.quant_rows(bf16_cu(g["x_bf16"]), mode=L.QI8_Q_BLOCK)
