@@ -62,9 +62,18 @@ def parse():
     ap.add_argument("--impl", default="qi8", choices=["qi8", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=512, help="token sample of the CPU baseline step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="dit_mlp", choices=["dit_mlp", "quip_linear", "conversion"],
+    ap.add_argument("--workload", default="dit_mlp",
+                    choices=["dit_mlp", "quip_linear", "conversion", "flux_stack", "t5_stack"],
                     help="dit_mlp: the headline DiT MLP pair; quip_linear: one rotated W8A8 linear "
-                         "(K1 rotate -> K2 -> K3); conversion: the 304-tensor QuIP conversion sweep")
+                         "(K1 rotate -> K2 -> K3); conversion: the 304-tensor QuIP conversion sweep; "
+                         "flux_stack / t5_stack: the 228-linear Flux-shaped / 168-linear T5-XXL stacks")
+    ap.add_argument("--shard", default="replica", choices=["replica", "columns"],
+                    help="stacks on N>1 GPUs: replica = one batch per rank (weak scaling); columns = every "
+                         "linear column-sharded with overlapped NCCL all-gathers (strong scaling)")
+    ap.add_argument("--chunks", type=int, default=4, help="token chunks per column-sharded linear (nccl gather)")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="column-sharded output gather: peer = fused into the GEMM epilogue (stores into every "
+                         "rank's IPC-mapped buffer + peer barrier); nccl = chunked NCCL all-gather + re-layout")
     return ap.parse_args()
 
 
@@ -339,6 +348,184 @@ def main_conversion(args):
     _finish(world)
 
 
+def cpu_stack_step_fn(name: str, tokens: int = 256):
+    """CPU oracle port of one linear of every distinct shape of a stack on a
+    ``tokens``-row sample; returns (callable, ops per call, description)."""
+    import oracle as O
+    from convert_to_quant_quip_int8_b200.stack import STACKS
+
+    cfg = STACKS[name]
+    shapes = sorted({(s.k, s.n, s.gelu) for s in cfg["specs"]()})
+    rng = np.random.default_rng(0)
+    cases = []
+    for k, n, gelu in shapes:
+        x = O.round_bf16(rng.standard_normal((tokens, k)).astype(np.float32))
+        wq, ws = O.quantize_int8_axiswise(O.round_bf16((rng.standard_normal((n, k)) * 0.02).astype(np.float32)))
+        b = O.round_bf16((rng.standard_normal(n) * 0.01).astype(np.float32)) if cfg["bias"] else None
+        cases.append((x, wq, ws.reshape(-1), b, gelu))
+
+    def step():
+        for x, wq, ws, b, gelu in cases:
+            xin = O.round_bf16(O.gelu_f32(x)) if gelu else x
+            O.f32_to_bf16(O.linear_w8a8(xin, wq, ws, b)[3])
+
+    ops = sum(2 * tokens * k * n for k, n, _ in shapes)
+    return step, ops, (f"one linear of each of the {len(shapes)} distinct shapes at {tokens} tokens "
+                       f"(numpy oracle port), scaled to the stack's ops per forward")
+
+
+def run_cpu_stack(name: str, steps: int, warmup: int):
+    """CPU tokens/s of the stack, extrapolated from the timed sample by ops."""
+    from convert_to_quant_quip_int8_b200.stack import STACKS, ops_per_forward
+
+    step, ops, sample = cpu_stack_step_fn(name)
+    for _ in range(max(0, warmup)):
+        step()
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    cfg = STACKS[name]
+    fwd_s = ops_per_forward(cfg["specs"]()) / (ops / med)
+    return cfg["tokens"] / fwd_s, med, sample
+
+
+def main_stack(args):
+    """Configs 3 and 4: a whole linear stack per step (K1 + K2 per linear),
+    captured once as a CUDA graph and replayed; tokens/s of the whole job."""
+    import torch.nn.functional as F
+    from convert_to_quant_quip_int8_b200 import _lib as L
+    from convert_to_quant_quip_int8_b200 import ops, sharding
+    from convert_to_quant_quip_int8_b200.comfy.quant_ops import QuantizedTensor
+    from convert_to_quant_quip_int8_b200.stack import STACKS, LinearStack, ops_per_forward
+
+    name = args.workload.split("_")[0]
+    cfg = STACKS[name]
+    rank, world, local = dist_init(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    shard = args.shard if world > 1 else "replica"
+    st = LinearStack(name, device, rank, world, shard, chunks=args.chunks, gather=args.gather)
+    warm = max(3, args.warmup)
+    for _ in range(2):
+        st.forward()
+    torch.cuda.synchronize(device)
+    ops.device_status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st.forward()
+    for _ in range(warm):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    ms, clocks = timed_region(graph.replay, args.steps, world, device)
+    ops.device_status()
+    ms_step = ms / args.steps
+    tokens = cfg["tokens"]
+    value = (world if shard == "replica" else 1) * tokens * args.steps / (ms / 1e3)
+    fwd_ops = ops_per_forward(st.specs)
+
+    # GEMM kernel time: one eager forward with CUDA events around every linear's GEMM launches
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in st.specs]
+    barrier(world)
+    st.forward(evs)
+    torch.cuda.synchronize(device)
+    gemm_ms = sum(a.elapsed_time(b) for a, b in evs)
+    gemm_ms = max_over_ranks(gemm_ms, world, device)
+    achieved = st.gemm_ops_local() / (gemm_ms / 1e3) / 1e12
+
+    # e2e through the public API: host inputs -> F.linear(x, QuantizedTensor) per linear -> host output
+    layout = "TensorWiseINT8Layout" if cfg["quip"] else "AxisWiseINT8Layout"
+    e2e_ws = None
+    if shard == "columns":
+        if args.gather == "peer":
+            max_tn = max(s.tokens * s.n for s in st.specs)
+            e2e_ws = sharding.PeerWorkspace(max_tn * 2, world, rank, device=device)
+        layers = [sharding.ColumnShardedW8A8Linear.from_local(q, sc, b, world, chunks=args.chunks, peer=e2e_ws)
+                  for q, sc, b in st.weights]
+        apply = lambda i, x: layers[i](x)
+    else:
+        qts = [QuantizedTensor(q, layout, {"scale": sc if not cfg["quip"] else sc.reshape(-1, 1),
+                                           "orig_dtype": torch.bfloat16}) for q, sc, _ in st.weights]
+        apply = lambda i, x: F.linear(x, qts[i], st.weights[i][2])
+    host_in = st.host_inputs()
+    last = st.specs[-1]
+    y_host = torch.empty(last.tokens, last.n, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_forward():
+        dev_in = {k: v.to(device, non_blocking=True) for k, v in host_in.items()}
+        kept, y = {}, None
+        for i, s in enumerate(st.specs):
+            x = dev_in[(s.tokens, s.k)] if s.src == "x" else F.gelu(kept.pop(s.src))
+            y = apply(i, x)
+            if any(t.src == s.name for t in st.specs):
+                kept[s.name] = y
+        y_host.copy_(y, non_blocking=True)
+
+    e2e_forward()
+    torch.cuda.synchronize(device)
+    e_steps = max(2, min(args.steps, 5))
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        e2e_forward()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device) / e_steps
+    e2e_value = (world if shard == "replica" else 1) * tokens / (e2e_ms / 1e3)
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    ops.device_status()
+    del graph
+    if e2e_ws is not None:
+        e2e_ws.close()
+    st.close()
+    if rank != 0:
+        _finish(world)
+        return
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
+    line = {
+        "metric": f"{name} W8A8 linear-stack tokens/s", "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warm, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak" if shard == "replica" else "strong", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 (fp32 epilogue, bf16 out)",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations"
+                + (", 1% Student-t(3) outlier channels)" if name == "t5" else ")"),
+        "config": {"workload": cfg["describe"], "tokens_per_forward": tokens, "linears": len(st.specs),
+                   "ops_per_forward": fwd_ops, "tops": round(fwd_ops * (world if shard == "replica" else 1)
+                                                             / (ms_step / 1e3) / 1e12, 1),
+                   "parallelism": ((f"column-sharded x{world}, output gather fused into the GEMM epilogue "
+                                    "(peer stores over NVLink + peer barrier)" if args.gather == "peer" else
+                                    f"column-sharded x{world}, {args.chunks} token chunks, NCCL all-gather")
+                                   if shard == "columns" else (f"replicas x{world}" if world > 1 else "single")),
+                   "graph": "one CUDA graph per forward",
+                   "l2": "inputs larger than L2: every forward streams 8.6 GB (flux) / 4.6 GB (t5) of int8 weights"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(last.tokens * last.n * 2), "ms_per_step": round(e2e_ms, 3),
+                "path": (f"ColumnShardedW8A8Linear ({args.gather} gather) per linear" if shard == "columns"
+                         else f"F.linear(x, QuantizedTensor[{layout}]) per linear") + ", pinned host in/out"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
+                     "frac": round(achieved / int8_peak, 4), "traffic": None,
+                     "kernel": "gemm_pair_kernel<false,false> (per-row scales; CUDA events around every GEMM "
+                               "of one eager forward" + (", incl. its peer stores)" if shard == "columns" and
+                                                         args.gather == "peer" else ")"),
+                     "peak_note": f"dense int8 = 2 x {peak_kind} cuBLAS bf16 sustained "
+                                  f"({peaks.get('bf16_tflops_sustained')} TF/s)",
+                     "gemm_ms_per_forward": round(gemm_ms, 3)},
+        "gpu_launches": st.launches_per_forward() * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        torch.set_num_threads(cpu_cores())
+        cv, cmed, sample = run_cpu_stack(name, 2, 1)
+        line["cpu_baseline"] = {"value": round(cv, 3), "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                                "sample": sample, "s_per_sample": round(cmed, 3)}
+    print(json.dumps(line), flush=True)
+    _finish(world)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -347,6 +534,8 @@ def main():
         return main_quip_linear(args)
     if args.workload == "conversion":
         return main_conversion(args)
+    if args.workload in ("flux_stack", "t5_stack"):
+        return main_stack(args)
     from convert_to_quant_quip_int8_b200 import _lib as L
     from convert_to_quant_quip_int8_b200 import ops
     from convert_to_quant_quip_int8_b200.comfy.quant_ops import QuantizedTensor
@@ -496,6 +685,45 @@ def _finish(world):
         torch.distributed.destroy_process_group()
 
 
+def cpu_other_workload(workload: str, steps: int, warmup: int):
+    """CPU oracle port of the quip_linear / conversion workloads on a bounded
+    sample; returns (metric, unit, value, seconds per sample, sample)."""
+    import oracle as O
+    from convert_to_quant_quip_int8_b200.workloads import SingleQuipLinear, conversion_sweep_tensors, quip_signs
+
+    if workload == "quip_linear":
+        wl = SingleQuipLinear()
+        su, sv = (t.numpy() for t in wl.signs())
+        qr, sr, _ = O.quip_convert(wl.weight().float().numpy(), su, sv, store_transformed=True)
+        x = wl.activations().float().numpy()[:128]
+        b = wl.bias().float().numpy()
+        step = lambda: O.quip_linear_w8a8(x, qr, sr, su, sv, wl.dim, b)
+        unit_ops, scale = 2 * 128 * wl.dim * wl.dim, None
+        metric, unit, sample = ("QuIP W8A8 rotated linear TOPS (transformed storage, tensorwise scale)", "TOPS",
+                                "128 of 512 tokens through K1 -> int32 GEMM -> K3 (numpy oracle port)")
+    else:
+        w = (np.random.default_rng(0).standard_normal((3072, 3072)) * 0.02).astype(np.float32)
+        su, sv = (t.numpy() for t in quip_signs(1000, 4096, 4096))
+        step = lambda: O.quip_convert(O.round_bf16(w), su, sv, "block")
+        shapes = [(m, n) for _, m, n in conversion_sweep_tensors()]
+        pad = lambda m, n: (1 << (m - 1).bit_length()) * (1 << (n - 1).bit_length())
+        scale = sum(pad(m, n) for m, n in shapes) / pad(3072, 3072)  # cost ~ padded elements
+        unit_ops = None
+        metric, unit, sample = ("QuIP conversion sweep tensors/s (304 tensors, 12.9 B params)", "tensors/s",
+                                "one 3072x3072 tensor (padded 4096x4096) through the numpy oracle converter, "
+                                "scaled to the sweep by padded element count")
+    for _ in range(max(0, warmup)):
+        step()
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    value = unit_ops / med / 1e12 if unit_ops else 304 / (med * scale)
+    return metric, unit, value, med, sample
+
+
 def main_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -503,17 +731,29 @@ def main_reference(args):
         return
     cores = cpu_cores()
     torch.set_num_threads(cores)
-    tokens = args.cpu_tokens
-    value, med, sample = run_cpu(tokens, args.steps, args.warmup)
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+    config = {"workload": WORKLOAD, "tokens": 4096, "hidden": 3072, "ffn": 12288, "block": 128,
+              "parallelism": "cpu"}
+    metric, unit, scaling = METRIC, UNIT, "weak"
+    if args.workload in ("flux_stack", "t5_stack"):
+        from convert_to_quant_quip_int8_b200.stack import STACKS
+        name = args.workload.split("_")[0]
+        value, med, sample = run_cpu_stack(name, args.steps, args.warmup)
+        metric, unit = f"{name} W8A8 linear-stack tokens/s", "tokens/s"
+        config = {"workload": STACKS[name]["describe"], "parallelism": "cpu"}
+        scaling = "weak" if args.shard == "replica" else "strong"
+    elif args.workload in ("quip_linear", "conversion"):
+        metric, unit, value, med, sample = cpu_other_workload(args.workload, args.steps, args.warmup)
+        config = {"workload": args.workload, "parallelism": "cpu"}
+        scaling = "weak" if args.workload == "quip_linear" else "strong"
+    else:
+        value, med, sample = run_cpu(args.cpu_tokens, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8 x int8 -> int32 (fp32 promote, bf16 out)", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": 4096, "hidden": 3072, "ffn": 12288, "block": 128,
-                       "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "int8 x int8 -> int32 (fp32 epilogue)", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores, "kind": "port",
                              "sample": sample},
-            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 

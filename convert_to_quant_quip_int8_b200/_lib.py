@@ -32,6 +32,7 @@ QI8_BF16, QI8_F16, QI8_F32, QI8_I8, QI8_I32 = 0, 1, 2, 3, 4
 QI8_Q_TOKEN, QI8_Q_BLOCK, QI8_Q_GELU = 0, 1, 0x100
 # scale kinds
 QI8_S_NONE, QI8_S_SCALAR, QI8_S_ROW, QI8_S_ROW_KBLOCK, QI8_S_TILE128 = 0, 1, 2, 3, 4
+QI8_MAX_PEERS = 8
 # epilogue activation
 QI8_ACT_NONE, QI8_ACT_GELU = 0, 1
 # weight requant schemes
@@ -64,6 +65,12 @@ SIGNATURES = {
     "qi8_requant_weight": (_I, [_P, _I, _I64, _I64, _I64, _I, _I, _P, _P, _P, _I64, _P]),
     "qi8_weight_rotate2d": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _I64, _P]),
     "qi8_allgather_cols": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "qi8_gather_layout": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P]),
+    "qi8_gemm_i8_gather": (_I, [_P, _P, _I64, _I64, _I64, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I, _I64, _I, _P]),
+    "qi8_ipc_handle": (_I, [_P, _P, ctypes.POINTER(_I64)]),
+    "qi8_ipc_open": (_I, [_P, _I64, ctypes.POINTER(_P)]),
+    "qi8_ipc_close": (_I, [_P, _I64]),
+    "qi8_peer_barrier": (_I, [_P, _I, _I, _P]),
 }
 
 _lib = None

@@ -86,6 +86,27 @@ bool nccl_dtype(int dtype, ncclDataType_t* t) {
 
 using namespace qi8;
 
+extern "C" int qi8_gather_layout(const void* gathered, int dtype, int world, int64_t rows, int64_t n_loc,
+                                 void* y_out, int64_t ld_out, void* stream) {
+  QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
+  QI8_REQUIRE(gathered && y_out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(world >= 1 && rows >= 0 && n_loc > 0, QI8_ESHAPE, "bad sizes world=%d rows=%lld n_loc=%lld", world,
+              (long long)rows, (long long)n_loc);
+  QI8_REQUIRE(ld_out >= (int64_t)world * n_loc, QI8_ESHAPE, "ld_out %lld < world * n_loc = %lld", (long long)ld_out,
+              (long long)world * n_loc);
+  const int es = elem_size(dtype);
+  QI8_REQUIRE(es > 0, QI8_EDTYPE, "dtype %d", dtype);
+  if (rows == 0) return QI8_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool vec = aligned16(gathered) && aligned16(y_out) && (n_loc * es) % 16 == 0 && (ld_out * es) % 16 == 0;
+  if (vec) return launch_layout<uint4>(gathered, y_out, rows, n_loc * es / 16, ld_out * es / 16, world, st);
+  switch (es) {
+    case 1: return launch_layout<uint8_t>(gathered, y_out, rows, n_loc, ld_out, world, st);
+    case 2: return launch_layout<uint16_t>(gathered, y_out, rows, n_loc, ld_out, world, st);
+    default: return launch_layout<uint32_t>(gathered, y_out, rows, n_loc, ld_out, world, st);
+  }
+}
+
 extern "C" int qi8_allgather_cols(const void* y_local, int dtype, int64_t rows, int64_t n_loc, void* y_out,
                                   int64_t ld_out, void* nccl_comm, void* scratch, int64_t scratch_bytes,
                                   void* stream) {
@@ -111,11 +132,5 @@ extern "C" int qi8_allgather_cols(const void* y_local, int dtype, int64_t rows, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   nr = api->all_gather(y_local, scratch, (size_t)(rows * n_loc), nt, comm, st);
   QI8_REQUIRE(nr == ncclSuccess, QI8_ECUDA, "ncclAllGather: %s", api->err_str(nr));
-  const bool vec = aligned16(scratch) && aligned16(y_out) && (n_loc * es) % 16 == 0 && (ld_out * es) % 16 == 0;
-  if (vec) return launch_layout<uint4>(scratch, y_out, rows, n_loc * es / 16, ld_out * es / 16, world, st);
-  switch (es) {
-    case 1: return launch_layout<uint8_t>(scratch, y_out, rows, n_loc, ld_out, world, st);
-    case 2: return launch_layout<uint16_t>(scratch, y_out, rows, n_loc, ld_out, world, st);
-    default: return launch_layout<uint32_t>(scratch, y_out, rows, n_loc, ld_out, world, st);
-  }
+  return qi8_gather_layout(scratch, dtype, world, rows, n_loc, y_out, ld_out, stream);
 }

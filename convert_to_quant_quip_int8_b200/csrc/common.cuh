@@ -44,6 +44,7 @@ enum : unsigned int {
   ST_GEMM_MMA = 1u << 1,
   ST_GEMM_EPILOGUE = 1u << 2,
   ST_GEMM_DRAIN = 1u << 3,
+  ST_PEER_BARRIER = 1u << 4,
 };
 
 // ---------------------------------------------------------- conversions

@@ -88,12 +88,27 @@ struct GemmArgs {
   int b_kind;
   const void* bias;
   int bias_dtype;
-  void* out;
+  // Output destinations, each [M, ld_out] from its own base: outs[0] on this
+  // device; outs[1..n_outs) peer-mapped copies (column-parallel gather),
+  // which receive the same tile at the same offset.
+  void* outs[QI8_MAX_PEERS];
+  int n_outs;
   int out_dtype;
   int64_t ld_out;
   int act;
   unsigned int* status;
 };
+
+// Calls f(base) for every output destination (static indices, so the
+// parameter struct stays in the constant bank).
+template <typename F>
+__device__ __forceinline__ void for_each_out(const GemmArgs& p, F&& f) {
+#pragma unroll
+  for (int d = 0; d < QI8_MAX_PEERS; ++d) {
+    if (d >= p.n_outs) break;
+    f(p.outs[d]);
+  }
+}
 
 // ------------------------------------------------------------- PTX glue
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -218,49 +233,53 @@ __device__ __forceinline__ float act_gelu(float y, int out_dtype) {
 __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, const float (&y)[32]) {
   const int64_t off = (int64_t)m * p.ld_out + n0;
   const bool full = (n0 + 32 <= p.N);
-  if (p.out_dtype == QI8_BF16) {
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + off;
+  if (p.out_dtype == QI8_BF16 || p.out_dtype == QI8_F16) {
+    const bool bf = p.out_dtype == QI8_BF16;
     if (full) {
+      uint4 u[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        uint4 u;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+        uint32_t* w = reinterpret_cast<uint32_t*>(&u[k]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[8 * k + 2 * j], y[8 * k + 2 * j + 1]);
-        reinterpret_cast<uint4*>(o)[k] = u;
+        for (int j = 0; j < 4; ++j) {
+          const float a = y[8 * k + 2 * j], b = y[8 * k + 2 * j + 1];
+          if (bf) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            w[j] = *reinterpret_cast<uint32_t*>(&h);
+          } else {
+            __half2 h = __floats2half2_rn(a, b);
+            w[j] = *reinterpret_cast<uint32_t*>(&h);
+          }
+        }
       }
+      for_each_out(p, [&](void* base) {
+        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = u[k];
+      });
     } else {
+      for_each_out(p, [&](void* base) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.N) o[j] = __float2bfloat16_rn(y[j]);
-    }
-  } else if (p.out_dtype == QI8_F16) {
-    __half* o = static_cast<__half*>(p.out) + off;
-    if (full) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint4 u;
-        __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(y[8 * k + 2 * j], y[8 * k + 2 * j + 1]);
-        reinterpret_cast<uint4*>(o)[k] = u;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.N) o[j] = __float2half_rn(y[j]);
+        for (int j = 0; j < 32; ++j) {
+          if (n0 + j >= p.N) continue;
+          if (bf) static_cast<__nv_bfloat16*>(base)[off + j] = __float2bfloat16_rn(y[j]);
+          else static_cast<__half*>(base)[off + j] = __float2half_rn(y[j]);
+        }
+      });
     }
   } else {
-    float* o = static_cast<float*>(p.out) + off;
-    if (full) {
+    for_each_out(p, [&](void* base) {
+      float* o = static_cast<float*>(base) + off;
+      if (full) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        reinterpret_cast<float4*>(o)[k] = make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
-    } else {
+        for (int k = 0; k < 8; ++k)
+          reinterpret_cast<float4*>(o)[k] = make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < p.N) o[j] = y[j];
-    }
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) o[j] = y[j];
+      }
+    });
   }
 }
 
@@ -268,47 +287,49 @@ __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, co
 __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, const float (&y)[8]) {
   const int64_t off = (int64_t)m * p.ld_out + n0;
   const bool full = (n0 + 8 <= p.N);
-  if (p.out_dtype == QI8_BF16) {
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + off;
+  if (p.out_dtype == QI8_BF16 || p.out_dtype == QI8_F16) {
+    const bool bf = p.out_dtype == QI8_BF16;
     if (full) {
       uint4 u;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+      uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
-      *reinterpret_cast<uint4*>(o) = u;
+      for (int j = 0; j < 4; ++j) {
+        if (bf) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      for_each_out(p, [&](void* base) { *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) = u; });
     } else {
+      for_each_out(p, [&](void* base) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (n0 + j < p.N) o[j] = __float2bfloat16_rn(y[j]);
-    }
-  } else if (p.out_dtype == QI8_F16) {
-    __half* o = static_cast<__half*>(p.out) + off;
-    if (full) {
-      uint4 u;
-      __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
-      *reinterpret_cast<uint4*>(o) = u;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (n0 + j < p.N) o[j] = __float2half_rn(y[j]);
+        for (int j = 0; j < 8; ++j) {
+          if (n0 + j >= p.N) continue;
+          if (bf) static_cast<__nv_bfloat16*>(base)[off + j] = __float2bfloat16_rn(y[j]);
+          else static_cast<__half*>(base)[off + j] = __float2half_rn(y[j]);
+        }
+      });
     }
   } else {
-    float* o = static_cast<float*>(p.out) + off;
-    if (full) {
-      reinterpret_cast<float4*>(o)[0] = make_float4(y[0], y[1], y[2], y[3]);
-      reinterpret_cast<float4*>(o)[1] = make_float4(y[4], y[5], y[6], y[7]);
-    } else {
+    for_each_out(p, [&](void* base) {
+      float* o = static_cast<float*>(base) + off;
+      if (full) {
+        reinterpret_cast<float4*>(o)[0] = make_float4(y[0], y[1], y[2], y[3]);
+        reinterpret_cast<float4*>(o)[1] = make_float4(y[4], y[5], y[6], y[7]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (n0 + j < p.N) o[j] = y[j];
-    }
+        for (int j = 0; j < 8; ++j)
+          if (n0 + j < p.N) o[j] = y[j];
+      }
+    });
   }
 }
 
 __device__ __forceinline__ void store_row32_i32(const GemmArgs& p, int m, int n0, const uint32_t (&r)[32]) {
-  int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)m * p.ld_out + n0;
+  int32_t* o = static_cast<int32_t*>(p.outs[0]) + (int64_t)m * p.ld_out + n0;  // int32 output: one destination
   if (n0 + 32 <= p.N) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) reinterpret_cast<uint4*>(o)[k] = make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
@@ -375,9 +396,12 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
         const int f0 = rr - lane + h * 16;  // first of the 16 features this lane stores
         if (tok < C && f0 < R) {
           const uint4* src = reinterpret_cast<const uint4*>(tb + t * 32 + h * 16);
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)tok * p.ld_out + f0);
-          dst[0] = src[0];
-          dst[1] = src[1];
+          const uint4 v0 = src[0], v1 = src[1];
+          for_each_out(p, [&](void* base) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + (int64_t)tok * p.ld_out + f0);
+            dst[0] = v0;
+            dst[1] = v1;
+          });
         }
       } else if (row_ok) {
 #pragma unroll
@@ -388,8 +412,10 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
           if (GELU) y = act_gelu(y, p.out_dtype);
           if (col0 + j < C) {
             const int64_t o = (int64_t)(col0 + j) * p.ld_out + rr;
-            if (p.out_dtype == QI8_F16) static_cast<__half*>(p.out)[o] = __float2half_rn(y);
-            else static_cast<float*>(p.out)[o] = y;
+            for_each_out(p, [&](void* base) {
+              if (p.out_dtype == QI8_F16) static_cast<__half*>(base)[o] = __float2half_rn(y);
+              else static_cast<float*>(base)[o] = y;
+            });
           }
         }
       }
@@ -1180,6 +1206,11 @@ int make_map(CUtensorMap* map, const int8_t* ptr, int64_t rows, int64_t K, uint3
 
 bool g_attr_set[3][64];
 
+void set_outs(GemmArgs& p, void* const* outs, int n_outs) {
+  for (int d = 0; d < QI8_MAX_PEERS; ++d) p.outs[d] = d < n_outs ? outs[d] : nullptr;
+  p.n_outs = n_outs;
+}
+
 // Launches the CTA-pair kernel; grid = 2 x min(tiles, co-resident clusters).
 template <bool PROMOTE, bool SWAP>
 int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, int dev, cudaStream_t st) {
@@ -1228,17 +1259,24 @@ int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs
 
 using namespace qi8;
 
-extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale,
-                           int a_kind, const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* out,
-                           int out_dtype, int64_t ld_out, int act, void* stream) {
+namespace qi8 {
+namespace {
+
+// Validates the GEMM and launches it; every destination in outs[0..n_outs)
+// receives the full [M, N] result at row stride ld_out.
+int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale, int a_kind,
+                const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* const* outs, int n_outs,
+                int out_dtype, int64_t ld_out, int act, void* stream) {
   QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
-  QI8_REQUIRE(A && B && out, QI8_EINVAL, "null pointer");
+  QI8_REQUIRE(A && B && outs && n_outs >= 1 && n_outs <= QI8_MAX_PEERS, QI8_EINVAL, "null pointer or bad n_outs");
+  for (int d = 0; d < n_outs; ++d) QI8_REQUIRE(outs[d], QI8_EINVAL, "null output pointer %d", d);
   QI8_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), QI8_ESHAPE,
               "bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
   QI8_REQUIRE(K % 16 == 0, QI8_ESHAPE, "K=%lld must be a multiple of 16", (long long)K);
   QI8_REQUIRE(N % 16 == 0, QI8_ESHAPE, "N=%lld must be a multiple of 16", (long long)N);
   QI8_REQUIRE(ld_out >= N, QI8_ESHAPE, "ld_out < N");
-  QI8_REQUIRE(aligned16(A) && aligned16(B) && aligned16(out), QI8_EALIGN, "A, B and out must be 16-byte aligned");
+  QI8_REQUIRE(aligned16(A) && aligned16(B), QI8_EALIGN, "A, B and out must be 16-byte aligned");
+  for (int d = 0; d < n_outs; ++d) QI8_REQUIRE(aligned16(outs[d]), QI8_EALIGN, "A, B and out must be 16-byte aligned");
   QI8_REQUIRE(a_kind >= QI8_S_NONE && a_kind <= QI8_S_ROW_KBLOCK, QI8_EINVAL, "a_kind %d", a_kind);
   QI8_REQUIRE(b_kind >= QI8_S_NONE && b_kind <= QI8_S_TILE128, QI8_EINVAL, "b_kind %d", b_kind);
   QI8_REQUIRE((a_kind == QI8_S_NONE) == (a_scale == nullptr), QI8_EINVAL, "a_scale/a_kind mismatch");
@@ -1251,6 +1289,7 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   QI8_REQUIRE((ld_out * es) % 16 == 0, QI8_EALIGN, "ld_out * elem_size must be a multiple of 16");
   const bool promote = a_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_TILE128;
   if (promote) QI8_REQUIRE(K % 128 == 0, QI8_ESHAPE, "block scales need K %% 128 == 0 (K=%lld)", (long long)K);
+  QI8_REQUIRE(out_dtype != QI8_I32 || n_outs == 1, QI8_EINVAL, "int32 output has one destination");
   if (out_dtype == QI8_I32)
     QI8_REQUIRE(!promote && a_kind == QI8_S_NONE && b_kind == QI8_S_NONE && !bias && act == QI8_ACT_NONE,
                 QI8_EINVAL, "int32 output takes no scales, bias or activation");
@@ -1274,7 +1313,8 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
     p.c_tiles = (int)((Crows + bnp - 1) / bnp);
     p.num_tiles = p.r_tiles * p.c_tiles;
     p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
-    p.bias = bias; p.bias_dtype = bias_dtype; p.out = out; p.out_dtype = out_dtype; p.ld_out = ld_out;
+    p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
+    set_outs(p, outs, n_outs);
     p.act = act;
     p.status = device_status_ptr();
     CUtensorMap mapA, mapB;
@@ -1298,7 +1338,8 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   p.c_tiles = (int)((Crows + BN - 1) / BN);
   p.num_tiles = p.r_tiles * p.c_tiles;
   p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
-  p.bias = bias; p.bias_dtype = bias_dtype; p.out = out; p.out_dtype = out_dtype; p.ld_out = ld_out;
+  p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
+    set_outs(p, outs, n_outs);
   p.act = act;
   p.status = device_status_ptr();
 
@@ -1327,4 +1368,37 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
                 cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes, SMEM_BYTES, grid);
   }
   return QI8_OK;
+}
+
+}  // namespace
+}  // namespace qi8
+
+extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                           int a_kind, const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* out,
+                           int out_dtype, int64_t ld_out, int act, void* stream) {
+  void* outs[1] = {out};
+  return gemm_launch(A, B, M, N, K, a_scale, a_kind, b_scale, b_kind, bias, bias_dtype, outs, 1, out_dtype, ld_out,
+                     act, stream);
+}
+
+extern "C" int qi8_gemm_i8_gather(const int8_t* A, const int8_t* B_local, int64_t M, int64_t n_loc, int64_t K,
+                                  const float* a_scale, int a_kind, const float* b_scale, int b_kind, const void* bias,
+                                  int bias_dtype, void* const* out_bases, int world, int rank, int out_dtype,
+                                  int64_t ld_out, int act, void* stream) {
+  QI8_REQUIRE(out_bases, QI8_EINVAL, "null out_bases");
+  QI8_REQUIRE(world >= 1 && world <= QI8_MAX_PEERS && rank >= 0 && rank < world, QI8_EINVAL,
+              "world %d / rank %d (at most %d ranks)", world, rank, QI8_MAX_PEERS);
+  QI8_REQUIRE(out_dtype == QI8_BF16 || out_dtype == QI8_F16 || out_dtype == QI8_F32, QI8_EDTYPE,
+              "gathered output dtype %d (bf16, f16 or f32)", out_dtype);
+  QI8_REQUIRE(n_loc > 0 && ld_out >= (int64_t)world * n_loc, QI8_ESHAPE, "ld_out %lld < world * n_loc = %lld",
+              (long long)ld_out, (long long)world * n_loc);
+  const int64_t col_bytes = (int64_t)rank * n_loc * elem_size(out_dtype);
+  // this device's own buffer first, then the peers in rank order
+  void* outs[QI8_MAX_PEERS];
+  int n = 0;
+  outs[n++] = static_cast<char*>(out_bases[rank]) + col_bytes;
+  for (int r = 0; r < world; ++r)
+    if (r != rank) outs[n++] = out_bases[r] ? static_cast<char*>(out_bases[r]) + col_bytes : nullptr;
+  return gemm_launch(A, B_local, M, n_loc, K, a_scale, a_kind, b_scale, b_kind, bias, bias_dtype, outs, world,
+                     out_dtype, ld_out, act, stream);
 }

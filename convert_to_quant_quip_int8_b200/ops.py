@@ -287,6 +287,21 @@ def allgather_cols(y_local: torch.Tensor, nccl_comm: int, world: int,
     return out
 
 
+def gather_layout(gathered: torch.Tensor, world: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``[world, T, n_loc]`` (or ``[world * T, n_loc]``) all-gather result ->
+    ``[T, world * n_loc]``; ``out`` may be a row-strided view."""
+    L.require_cuda(gathered)
+    assert gathered.is_contiguous(), "gathered must be contiguous"
+    n_loc = gathered.shape[-1]
+    T = gathered.numel() // (world * n_loc)
+    if out is None:
+        out = torch.empty((T, world * n_loc), dtype=gathered.dtype, device=gathered.device)
+    assert out.shape == (T, world * n_loc) and out.stride(1) == 1, "out must be [T, world * n_loc] row-major"
+    L.check(L.load().qi8_gather_layout(L.ptr(gathered), L.dtype_code(gathered.dtype), world, T, n_loc, L.ptr(out),
+                                       out.stride(0), L.stream_ptr(gathered.device)), "qi8_gather_layout")
+    return out
+
+
 def requant_weight(w: torch.Tensor, requant: int = L.QI8_REQ_ROW, block: int = 128):
     """QuIP requant rule without rotation (converters/quip_int8.py:1614-1669)."""
     L.require_cuda(w)

@@ -1,0 +1,265 @@
+"""Device-resident W8A8 linear stacks (the Flux-shaped transformer and the
+T5-XXL encoder), run through the C ABI with preallocated buffers so that a
+whole forward can be captured once and replayed as a CUDA graph.
+
+* ``flux``: hidden 3072; 19 double-stream blocks x {img T=4096, txt T=512} x
+  {qkv 3072->9216, proj 3072->3072, mlp0 3072->12288, mlp2 12288->3072} and
+  38 single-stream blocks (T=4608) x {linear1 3072->21504, linear2
+  15360->3072} = 228 linears with bias.  QuIP W8A8 tensorwise weights: the
+  two-sided Hadamard conversion with the converter's default per-row requant
+  scale ``[N, 1]`` (converters/quip_int8.py:1639-1642), stored in original
+  space.
+* ``t5``: d_model 4096, d_ff 10240, 24 layers x {q, k, v, o 4096->4096,
+  wi_0, wi_1 4096->10240, wo 10240->4096} = 168 linears without bias, batch
+  8 x 512 tokens; axis-wise weight scales ``[N]``
+  (``AxisWiseINT8Layout``, comfy/quant_ops.py:330-339).
+
+Each linear is the reference's W8A8 forward (comfy/quant_ops.py:461-475):
+per-token int8 quantization of the bf16 input (K1), then the int8 GEMM with
+the fused ``acc * (x_s * w_s) + bias`` epilogue (K2) to bf16.  Inputs are
+seeded synthetic activations resident in HBM, one per input shape, except
+the Flux MLP down projections, which read GELU(up projection) through K1's
+fused GELU.  Attention, norms and modulation are outside the stack.
+
+Multi-GPU (one process per GPU):
+* ``replica``: every rank runs the whole stack on its own batch.
+* ``columns``: every linear is column-sharded -- rank r holds weight rows
+  ``[r N/G, (r+1) N/G)`` -- and K1 runs on every rank.  ``gather="peer"``:
+  the GEMM epilogue stores each tile into every rank's peer-mapped output
+  buffer (``qi8_gemm_i8_gather``) and a peer barrier follows.
+  ``gather="nccl"``: the local GEMM runs in token chunks whose NCCL
+  all-gathers overlap the next chunk and ``qi8_gather_layout`` assembles
+  ``[T, N]`` on every rank.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from . import ops
+from .sharding import PeerWorkspace, token_chunks
+from .workloads import flux_linears, gen, next_pow2, student_t_outliers, t5_linears
+
+
+@dataclass
+class LinearSpec:
+    name: str
+    tokens: int
+    k: int
+    n: int
+    src: str = "x"      # "x": synthetic activation [tokens, k]; otherwise the linear whose output feeds this one
+    gelu: bool = False  # GELU of the input, fused into the per-token quantization
+
+
+def flux_specs() -> List[LinearSpec]:
+    specs = []
+    for name, t, k, n in flux_linears():
+        if name.endswith(".mlp2"):
+            specs.append(LinearSpec(name, t, k, n, name[: -len("mlp2")] + "mlp0", True))
+        else:
+            specs.append(LinearSpec(name, t, k, n))
+    return specs
+
+
+def t5_specs() -> List[LinearSpec]:
+    return [LinearSpec(name, t, k, n) for name, t, k, n in t5_linears()]
+
+
+STACKS = {
+    "flux": dict(specs=flux_specs, tokens=4096 + 512, bias=True, quip=True, w_seed=20, x_seed=100,
+                 describe="Flux-shaped stack: 19 double blocks (img 4096 + txt 512 tokens) + 38 single blocks "
+                          "(4608 tokens), 228 QuIP W8A8 linears, per-row [N,1] scales, bias"),
+    "t5": dict(specs=t5_specs, tokens=8 * 512, bias=False, quip=False, w_seed=32, x_seed=30,
+               describe="T5-XXL encoder: 24 layers x {q,k,v,o 4096->4096, wi_0/wi_1 4096->10240, "
+                        "wo 10240->4096}, 4096 tokens, axis-wise [N] scales"),
+}
+
+
+def ops_per_forward(specs: List[LinearSpec]) -> int:
+    return sum(2 * s.tokens * s.k * s.n for s in specs)
+
+
+class LinearStack:
+    """One stack on one rank: int8 weights (full, or this rank's column
+    shard), synthetic inputs and every intermediate buffer, preallocated."""
+
+    def __init__(self, name: str, device: torch.device, rank: int = 0, world: int = 1, shard: str = "replica",
+                 chunks: int = 4, group=None, specs: Optional[List[LinearSpec]] = None, gather: str = "peer"):
+        cfg = STACKS[name]
+        self.name, self.cfg, self.device = name, cfg, device
+        self.specs = cfg["specs"]() if specs is None else list(specs)
+        self.rank, self.world, self.group = rank, world, group
+        self.sharded = shard == "columns" and world > 1
+        self.chunks = chunks
+        self.gather = gather  # column mode: "peer" (fused into the GEMM epilogue) or "nccl"
+        self.peer = None
+        self.lib = L.load()
+        self._build_weights()
+        self._build_buffers()
+
+    # ------------------------------------------------------------ weights
+    def _build_weights(self):
+        cfg, dev = self.cfg, self.device
+        g = torch.Generator(device=dev)
+        ws = None
+        if cfg["quip"]:
+            max_ws = max(ops.quip_workspace_bytes(s.n, s.k) for s in self.specs)
+            ws = torch.empty(max_ws, dtype=torch.uint8, device=dev)
+        self.weights: List[Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]] = []
+        for i, s in enumerate(self.specs):
+            g.manual_seed(cfg["w_seed"] + i)
+            w = (torch.randn(s.n, s.k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            if cfg["quip"]:
+                g.manual_seed(2000 + i)
+                su = (torch.randint(0, 2, (next_pow2(s.n),), generator=g, device=dev) * 2 - 1).float()
+                sv = (torch.randint(0, 2, (next_pow2(s.k),), generator=g, device=dev) * 2 - 1).float()
+                q, sc, _ = ops.quip_convert(w, su, sv, requant=L.QI8_REQ_ROW, want_dequant=False, workspace=ws)
+            else:
+                q, sc = ops.quant_weight(w, L.QI8_S_ROW)
+            del w
+            sc = sc.reshape(s.n)
+            bias = None
+            if cfg["bias"]:
+                g.manual_seed(5000 + i)
+                bias = (torch.randn(s.n, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+            if self.sharded:
+                assert s.n % (16 * self.world) == 0, f"{s.name}: N={s.n} does not split over {self.world} ranks"
+                n_loc = s.n // self.world
+                rows = slice(self.rank * n_loc, (self.rank + 1) * n_loc)
+                q, sc = q[rows].contiguous(), sc[rows].contiguous()
+                bias = None if bias is None else bias[rows].contiguous()
+            self.weights.append((q, sc, bias))
+        torch.cuda.synchronize(dev)
+
+    # ------------------------------------------------------------ buffers
+    def _build_buffers(self):
+        dev, cfg = self.device, self.cfg
+        consumed = {s.src for s in self.specs if s.src != "x"}
+        self.inputs: Dict[Tuple[int, int], torch.Tensor] = {}
+        for s in self.specs:
+            key = (s.tokens, s.k)
+            if s.src == "x" and key not in self.inputs:
+                seed = cfg["x_seed"] + len(self.inputs)
+                if self.name == "t5":
+                    x = student_t_outliers(torch.randn(s.tokens, s.k, generator=gen(seed)), 0.01, 3, seed + 1)
+                    self.inputs[key] = x.to(torch.bfloat16).to(dev)
+                else:
+                    g = torch.Generator(device=dev)
+                    g.manual_seed(seed)
+                    self.inputs[key] = torch.randn(s.tokens, s.k, generator=g, device=dev).to(torch.bfloat16)
+        max_tk = max(s.tokens * s.k for s in self.specs)
+        max_t = max(s.tokens for s in self.specs)
+        max_tn = max(s.tokens * s.n for s in self.specs)
+        self.xq = torch.empty(max_tk, dtype=torch.int8, device=dev)
+        self.xs = torch.empty(max_t, dtype=torch.float32, device=dev)
+        # consumed outputs get their own buffer per (tokens, n); the rest share a scratch
+        keys = []
+        for s in self.specs:
+            if s.name in consumed and (s.tokens, s.n) not in keys:
+                keys.append((s.tokens, s.n))
+        if self.sharded and self.gather == "peer":
+            # every output lives in a peer-mapped buffer: the scratch is buffer 0, kept outputs follow
+            self.peer = PeerWorkspace(max_tn * 2, self.world, self.rank, self.group, 1 + len(keys), dev)
+            self.peer_index = {k: 1 + i for i, k in enumerate(keys)}
+            self.kept = {k: self.peer.buffer(1 + i, k, torch.bfloat16) for i, k in enumerate(keys)}
+            self.scratch = self.peer.bufs[0].view(torch.bfloat16)
+        else:
+            self.kept = {k: torch.empty(*k, dtype=torch.bfloat16, device=dev) for k in keys}
+            self.scratch = torch.empty(max_tn, dtype=torch.bfloat16, device=dev)
+        self.out_of = {}
+        for s in self.specs:
+            buf = self.kept.get((s.tokens, s.n)) if s.name in consumed else None
+            self.out_of[s.name] = buf if buf is not None else self.scratch[: s.tokens * s.n].view(s.tokens, s.n)
+        self.buf_index = {s.name: (self.peer_index[(s.tokens, s.n)] if self.peer is not None and s.name in consumed
+                                   else 0) for s in self.specs}
+        if self.sharded and self.gather == "nccl":
+            max_tnl = max(s.tokens * (s.n // self.world) for s in self.specs)
+            self.y_loc = torch.empty(max_tnl, dtype=torch.bfloat16, device=dev)
+            self.gathered = torch.empty(max_tn, dtype=torch.bfloat16, device=dev)
+
+    def source(self, s: LinearSpec) -> torch.Tensor:
+        return self.inputs[(s.tokens, s.k)] if s.src == "x" else self.out_of[s.src]
+
+    # ------------------------------------------------------------ forward
+    def _k1(self, x: torch.Tensor, s: LinearSpec, sp):
+        mode = L.QI8_Q_TOKEN | (L.QI8_Q_GELU if s.gelu else 0)
+        L.check(self.lib.qi8_quant_rows(L.ptr(x), L.QI8_BF16, s.tokens, s.k, s.k, mode, 128, L.ptr(self.xq), s.k,
+                                        L.ptr(self.xs), sp), "qi8_quant_rows")
+
+    def _gemm(self, i: int, s: LinearSpec, lo: int, hi: int, out_ptr: int, ld_out: int, sp):
+        q, sc, bias = self.weights[i]
+        n = q.shape[0]
+        a = self.xq.data_ptr() + lo * s.k
+        xs = self.xs.data_ptr() + lo * 4
+        L.check(self.lib.qi8_gemm_i8(ctypes.c_void_p(a), L.ptr(q), hi - lo, n, s.k, ctypes.c_void_p(xs), L.QI8_S_ROW,
+                                     L.ptr(sc), L.QI8_S_ROW, L.ptr(bias), L.QI8_BF16 if bias is not None else 0,
+                                     ctypes.c_void_p(out_ptr), L.QI8_BF16, ld_out, L.QI8_ACT_NONE, sp), "qi8_gemm_i8")
+
+    def run_linear(self, i: int, sp, events=None):
+        s = self.specs[i]
+        self._k1(self.source(s), s, sp)
+        out = self.out_of[s.name]
+        if events is not None:
+            events[0].record()
+        if not self.sharded:
+            self._gemm(i, s, 0, s.tokens, out.data_ptr(), s.n, sp)
+            if events is not None:
+                events[1].record()
+            return
+        n_loc = s.n // self.world
+        if self.peer is not None:
+            q, sc, bias = self.weights[i]
+            xq = self.xq[: s.tokens * s.k].view(s.tokens, s.k)
+            L.check(self.lib.qi8_gemm_i8_gather(
+                L.ptr(xq), L.ptr(q), s.tokens, n_loc, s.k, L.ptr(self.xs), L.QI8_S_ROW, L.ptr(sc), L.QI8_S_ROW,
+                L.ptr(bias), L.QI8_BF16 if bias is not None else 0, self.peer.out_bases(self.buf_index[s.name]),
+                self.world, self.rank, L.QI8_BF16, s.n, L.QI8_ACT_NONE, sp), "qi8_gemm_i8_gather")
+            if events is not None:
+                events[1].record()
+            self.peer.barrier(sp)
+            return
+        y_loc = self.y_loc[: s.tokens * n_loc].view(s.tokens, n_loc)
+        gathered = self.gathered[: s.tokens * s.n]
+        pending = []
+        for lo, hi in token_chunks(s.tokens, self.chunks):
+            self._gemm(i, s, lo, hi, y_loc[lo:hi].data_ptr(), n_loc, sp)
+            buf = gathered[lo * s.n: hi * s.n].view(self.world * (hi - lo), n_loc)
+            pending.append((dist.all_gather_into_tensor(buf, y_loc[lo:hi], group=self.group, async_op=True),
+                            buf, lo, hi))
+        if events is not None:
+            events[1].record()
+        for work, buf, lo, hi in pending:
+            work.wait()
+            L.check(self.lib.qi8_gather_layout(L.ptr(buf), L.QI8_BF16, self.world, hi - lo, n_loc,
+                                               ctypes.c_void_p(out[lo:hi].data_ptr()), s.n, sp),
+                    "qi8_gather_layout")
+
+    def forward(self, events=None):
+        sp = L.stream_ptr(self.device)
+        for i in range(len(self.specs)):
+            self.run_linear(i, sp, None if events is None else events[i])
+
+    def launches_per_forward(self) -> int:
+        """Kernels of this library launched by one forward (K1 + GEMMs + layouts)."""
+        if not self.sharded:
+            return 2 * len(self.specs)
+        if self.peer is not None:
+            return 3 * len(self.specs)  # K1, fused GEMM + gather, peer barrier
+        return sum(1 + 2 * len(token_chunks(s.tokens, self.chunks)) for s in self.specs)
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+
+    def gemm_ops_local(self) -> int:
+        """Multiply-add ops of this rank's GEMMs per forward."""
+        return sum(2 * s.tokens * s.k * w[0].shape[0] for s, w in zip(self.specs, self.weights))
+
+    def host_inputs(self) -> Dict[Tuple[int, int], torch.Tensor]:
+        return {k: v.cpu().pin_memory() for k, v in self.inputs.items()}

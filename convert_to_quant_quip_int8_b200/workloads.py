@@ -124,3 +124,33 @@ def conversion_sweep_tensors() -> List[Tuple[str, int, int]]:
         for b in range(38):
             out += [(f"single{b}.{rep}.linear1", 21504, 3072), (f"single{b}.{rep}.linear2", 3072, 15360)]
     return out
+
+
+# ---------------------------------------------------- T5-XXL encoder stack
+def t5_linears() -> List[Tuple[str, int, int, int]]:
+    """(name, tokens, in_features, out_features) of the 168 linears of a
+    T5-XXL-shaped encoder forward (d_model 4096, d_ff 10240, 24 layers,
+    batch 8 x 512 tokens): q, k, v, o 4096->4096, gated-GELU wi_0 / wi_1
+    4096->10240 and wo 10240->4096."""
+    t = 8 * 512
+    out = []
+    for layer in range(24):
+        pre = f"encoder{layer}"
+        out += [(f"{pre}.q", t, 4096, 4096), (f"{pre}.k", t, 4096, 4096), (f"{pre}.v", t, 4096, 4096),
+                (f"{pre}.o", t, 4096, 4096), (f"{pre}.wi_0", t, 4096, 10240), (f"{pre}.wi_1", t, 4096, 10240),
+                (f"{pre}.wo", t, 10240, 4096)]
+    return out
+
+
+def student_t_outliers(x: torch.Tensor, frac: float, nu: int, seed: int) -> torch.Tensor:
+    """Replaces ``frac`` of the channels of ``x`` [T, C] by Student-t(nu)
+    samples (heavy-tailed outlier channels), seeded on the CPU."""
+    g = gen(seed)
+    n_ch = max(1, round(frac * x.shape[-1]))
+    idx = torch.randperm(x.shape[-1], generator=g)[:n_ch]
+    # Student-t(nu) = N(0,1) / sqrt(chi2(nu) / nu); chi2 of integer nu = sum of nu squared N(0,1)
+    z = torch.randn(x.shape[0], n_ch, generator=g)
+    chi2 = (torch.randn(int(nu), x.shape[0], n_ch, generator=g) ** 2).sum(0)
+    x = x.clone()
+    x[:, idx] = (z / torch.sqrt(chi2 / nu)).to(x.dtype)
+    return x

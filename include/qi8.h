@@ -26,6 +26,10 @@ extern "C" {
 
 #define QI8_ABI_VERSION 1
 
+/* Largest number of ranks (output destinations) of the column-parallel
+   entry points (qi8_gemm_i8_gather, qi8_peer_barrier). */
+#define QI8_MAX_PEERS 8
+
 #if defined(__GNUC__)
 #define QI8_API __attribute__((visibility("default")))
 #else
@@ -231,6 +235,49 @@ QI8_API int qi8_weight_rotate2d(const void* w, int w_dtype, int64_t M, int64_t N
 QI8_API int qi8_allgather_cols(const void* y_local, int dtype, int64_t rows, int64_t n_loc, void* y_out,
                                int64_t ld_out, void* nccl_comm, void* scratch, int64_t scratch_bytes,
                                void* stream);
+
+/* Re-layout of an all-gather result: gathered [G, rows, n_loc] (rank-major,
+   as ncclAllGather leaves it) -> Y [rows, G*n_loc] with row stride ld_out,
+   Y[t, r*n_loc + j] = gathered[r, t, j].  For callers that run the
+   collective themselves (e.g. torch.distributed, per token chunk).  Any
+   1/2/4-byte dtype; 16-byte vector copies when every row start is 16-byte
+   aligned. */
+QI8_API int qi8_gather_layout(const void* gathered, int dtype, int world, int64_t rows, int64_t n_loc,
+                              void* y_out, int64_t ld_out, void* stream);
+
+/* Column-parallel K2 with the output all-gather fused into the epilogue
+   (multi-GPU inference, one process per GPU).  Rank `rank` of `world` holds
+   weight rows [rank*n_loc, (rank+1)*n_loc) as B_local [n_loc, K] (scales and
+   bias sliced the same way); out_bases[r] is rank r's output buffer Y
+   [M, ld_out] (ld_out >= world*n_loc) mapped into this process
+   (qi8_ipc_open; out_bases[rank] is the local buffer).  The epilogue stores
+   this rank's [M, n_loc] tile at column rank*n_loc of every rank's Y with
+   plain stores over NVLink, so after qi8_peer_barrier every rank holds the
+   whole Y.  Scales, bias, activation and dtypes as qi8_gemm_i8 (bf16 / f16 /
+   f32 output).  Replaces the GEMM + ncclAllGather + re-layout sequence of
+   the column-parallel plan (the reference runs these linears on one GPU,
+   comfy/quant_ops.py:461-475). */
+QI8_API int qi8_gemm_i8_gather(const int8_t* A, const int8_t* B_local, int64_t M, int64_t n_loc, int64_t K,
+                               const float* a_scale, int a_kind, const float* b_scale, int b_kind, const void* bias,
+                               int bias_dtype, void* const* out_bases, int world, int rank, int out_dtype,
+                               int64_t ld_out, int act, void* stream);
+
+/* CUDA IPC export of the allocation holding `ptr`: handle_out receives the
+   64-byte cudaIpcMemHandle_t of the allocation's base, offset_out the byte
+   offset of ptr inside it. */
+QI8_API int qi8_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+/* Maps a peer's exported allocation into this process (peer access enabled
+   on demand); *ptr_out = mapped base + offset. */
+QI8_API int qi8_ipc_open(const void* handle, int64_t offset, void** ptr_out);
+/* Unmaps a pointer returned by qi8_ipc_open (same offset). */
+QI8_API int qi8_ipc_close(void* ptr, int64_t offset);
+
+/* Stream-ordered barrier of `world` ranks over peer memory: flags[r] points
+   to rank r's QI8_MAX_PEERS + 1 uint32 flag words (zeroed by their owner
+   before the first barrier), mapped into this process.  Every rank must call
+   it the same number of times.  Waits at most 2 s, then sets a status bit
+   (reported as QI8_ETIMEOUT by qi8_device_status) and returns. */
+QI8_API int qi8_peer_barrier(uint32_t* const* flags, int world, int rank, void* stream);
 
 /* Original-space requantization of a weight W[M,N] (row stride ld_w) with the
    QuIP requant rule (converters/quip_int8.py:1614-1669): scale =

@@ -206,7 +206,7 @@ def test_column_sharded_linear_overlapped_chunks(kind):
     # the chunked GEMM + asynchronous all-gather path over a one-rank NCCL group
     import torch.distributed as dist
     r = np.random.default_rng(6)
-    x = torch.from_numpy(r.standard_normal((48, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
+    x = torch.from_numpy(r.standard_normal((1000, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
     w = (torch.from_numpy(r.standard_normal((512, 512)).astype(np.float32)) * 0.02).cuda()
     bias = torch.from_numpy(r.standard_normal(512).astype(np.float32)).to(torch.bfloat16).cuda()
     q, s = ops.requant_weight(w, L.QI8_REQ_ROW if kind == "row" else L.QI8_REQ_BLOCK)
@@ -215,7 +215,7 @@ def test_column_sharded_linear_overlapped_chunks(kind):
                             device_id=torch.device("cuda", 0))
     try:
         lin = sharding.ColumnShardedW8A8Linear(q, s, bias, rank=0, world=1, chunks=4)
-        assert lin.chunks == 4
+        assert lin.chunks == 4 and len(sharding.token_chunks(1000, 4)) == 4
         y = lin(x)
         torch.cuda.synchronize()
     finally:

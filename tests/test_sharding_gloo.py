@@ -27,6 +27,13 @@ def _init(rank, world, port, timeout_s=20):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
 
 
+def _torch_layout(gathered, world, out):
+    """CPU statement of qi8_gather_layout: [G*T, n] -> out[t, r*n + j] = gathered[r*T + t, j]."""
+    T = out.shape[0]
+    out.copy_(gathered.view(world, T, -1).permute(1, 0, 2).reshape(T, -1))
+    return out
+
+
 def _worker_plan(rank, world, port, q):
     try:
         _init(rank, world, port)
@@ -38,9 +45,12 @@ def _worker_plan(rank, world, port, q):
         # column all-gather layout: rank r contributes columns r*4 .. r*4+3
         T = 3
         y_local = torch.arange(T * 4, dtype=torch.float32).reshape(T, 4) + 100 * rank
-        y = sharding.gather_columns(y_local, world)
-        # overlapped chunked gather: chunk k of rank r = columns k*2 .. k*2+1 of its shard
-        y_chunked = sharding.gather_columns_overlapped(lambda k: y_local[:, 2 * k:2 * k + 2], 2, world)
+        y = sharding.gather_columns(y_local, world, layout=_torch_layout)
+        # overlapped gather in token chunks (unit 1 token here): chunk = rows lo:hi of the shard
+        chunks = sharding.token_chunks(T, 2, unit=1)
+        assert chunks == [(0, 2), (2, 3)]
+        y_chunked = sharding.gather_rows_overlapped(lambda lo, hi: y_local[lo:hi], T, 2, world,
+                                                    layout=_torch_layout, unit=1)
         q.put((rank, everyone, y, y_chunked))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
