@@ -66,6 +66,8 @@ SIGNATURES = {
     "qi8_weight_rotate2d": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _I64, _P]),
     "qi8_allgather_cols": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _P, _I64, _P]),
     "qi8_gather_layout": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P]),
+    "qi8_gemm_workspace_bytes": (_I64, [_I64, _I64, _I64, _I, _I]),
+    "qi8_gemm_i8_ws": (_I, [_P, _P, _I64, _I64, _I64, _P, _I, _P, _I, _P, _I, _P, _I, _I64, _I, _P, _I64, _P]),
     "qi8_gemm_i8_gather": (_I, [_P, _P, _I64, _I64, _I64, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I, _I64, _I, _P]),
     "qi8_ipc_handle": (_I, [_P, _P, ctypes.POINTER(_I64)]),
     "qi8_ipc_open": (_I, [_P, _I64, ctypes.POINTER(_P)]),

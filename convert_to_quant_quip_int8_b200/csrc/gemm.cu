@@ -97,6 +97,11 @@ struct GemmArgs {
   int64_t ld_out;
   int act;
   unsigned int* status;
+  // split-K (plain path of the pair kernel): tile t covers K blocks
+  // [s * kb_split, (s + 1) * kb_split) of split s = t / (r_tiles * c_tiles) and
+  // stores its raw int32 sums to plane s (split_stride elements apart)
+  int kb_split;
+  int64_t split_stride;
 };
 
 // Calls f(base) for every output destination (static indices, so the
@@ -328,8 +333,9 @@ __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, con
   }
 }
 
-__device__ __forceinline__ void store_row32_i32(const GemmArgs& p, int m, int n0, const uint32_t (&r)[32]) {
-  int32_t* o = static_cast<int32_t*>(p.outs[0]) + (int64_t)m * p.ld_out + n0;  // int32 output: one destination
+__device__ __forceinline__ void store_row32_i32(const GemmArgs& p, int m, int n0, const uint32_t (&r)[32],
+                                                int64_t plane = 0) {
+  int32_t* o = static_cast<int32_t*>(p.outs[0]) + plane + (int64_t)m * p.ld_out + n0;  // int32: one destination
   if (n0 + 32 <= p.N) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) reinterpret_cast<uint4*>(o)[k] = make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
@@ -923,6 +929,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int KB = p.KB;
   const int r_ptiles = p.r_tiles;  // tiles of 256 rows over the TMEM-lane operand
+  const int rc_tiles = p.r_tiles * p.c_tiles;
   if (warp >= NUM_EPI_WARPS) {
     if constexpr (PROMOTE) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CTRL_REGS));
     if (warp == PRODUCER_WARP) {
@@ -932,9 +939,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
-          const int r0 = (tile % r_ptiles) * 256 + (int)rank * 128;
-          const int c0 = (tile / r_ptiles) * PBN + (int)rank * B_HALF;
-          for (int kb = 0; kb < KB; ++kb) {
+          const int rc = tile % rc_tiles, kb_lo = (tile / rc_tiles) * p.kb_split;
+          const int kb_hi = kb_lo + p.kb_split < KB ? kb_lo + p.kb_split : KB;
+          const int r0 = (rc % r_ptiles) * 256 + (int)rank * 128;
+          const int c0 = (rc / r_ptiles) * PBN + (int)rank * B_HALF;
+          for (int kb = kb_lo; kb < kb_hi; ++kb) {
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.status, ST_GEMM_PRODUCER, WAIT_LIMIT_NS)) {
               ok = false;
               break;
@@ -966,7 +975,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             const uint32_t d = tmem_base + (uint32_t)(buf * PBN);
-            const int kb_n = PROMOTE ? 1 : KB;
+            const int kb_lo = (tile / rc_tiles) * p.kb_split;
+            const int kb_n = PROMOTE ? 1 : (kb_lo + p.kb_split < KB ? p.kb_split : KB - kb_lo);
             for (int kb = 0; kb < kb_n; ++kb) {
               if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
                 ok = false;
@@ -1008,8 +1018,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int au = 0;
     bool ok = true;
     for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
-      const int rr = (tile % r_ptiles) * 256 + (int)rank * 128 + quad * 32 + lane;
-      const int c0 = (tile / r_ptiles) * PBN;
+      const int rc = tile % rc_tiles;
+      const int64_t plane = (int64_t)(tile / rc_tiles) * p.split_stride;
+      const int rr = (rc % r_ptiles) * 256 + (int)rank * 128 + quad * 32 + lane;
+      const int c0 = (rc / r_ptiles) * PBN;
       // this warp's 128 accumulator columns (output columns cc0 .. cc0 + 127)
       const int cc0 = c0 + cg * 128;
       const int cc1 = cc0 + 64;
@@ -1142,7 +1154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int n0 = cc0 + cc;
             if (!row_ok || n0 >= p.N) continue;
             if (p.out_dtype == QI8_I32) {
-              store_row32_i32(p, rr, n0, r[c]);
+              store_row32_i32(p, rr, n0, r[c], plane);
             } else {
               float y[32];
 #pragma unroll
@@ -1211,20 +1223,25 @@ void set_outs(GemmArgs& p, void* const* outs, int n_outs) {
   p.n_outs = n_outs;
 }
 
-// Launches the CTA-pair kernel; grid = 2 x min(tiles, co-resident clusters).
+// Co-resident CTA pairs of the pair kernel on device `dev` (queried once;
+// 0 with the error set when the kernel cannot run there).
 template <bool PROMOTE, bool SWAP>
-int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, int dev, cudaStream_t st) {
+int pair_max_clusters(int dev) {
   auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP>;
   static int max_clusters[64];
   if (dev < 0 || dev >= 64) dev = 0;
   if (max_clusters[dev] == 0) {
-    QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pairk::P_SMEM));
+    if (check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pairk::P_SMEM),
+                   "cudaFuncSetAttribute"))
+      return 0;
     if (PROMOTE) {
       cudaFuncAttributes fa{};
-      QI8_CUDA(cudaFuncGetAttributes(&fa, kern));
-      QI8_REQUIRE(fa.numRegs == LAUNCH_REGS, QI8_EUNSUPPORTED,
-                  "block-scaled GEMM compiled with %d registers per thread, register split needs %d", fa.numRegs,
-                  LAUNCH_REGS);
+      if (check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes")) return 0;
+      if (fa.numRegs != LAUNCH_REGS) {
+        fail(QI8_EUNSUPPORTED, "block-scaled GEMM compiled with %d registers per thread, register split needs %d",
+             fa.numRegs, LAUNCH_REGS);
+        return 0;
+      }
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * (sm_count() > 0 ? sm_count() / 2 : 74), 1, 1);
@@ -1238,11 +1255,23 @@ int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    QI8_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-    QI8_REQUIRE(n > 0, QI8_EUNSUPPORTED, "no CTA pair of the GEMM fits on the device");
+    if (check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "cudaOccupancyMaxActiveClusters")) return 0;
+    if (n <= 0) {
+      fail(QI8_EUNSUPPORTED, "no CTA pair of the GEMM fits on the device");
+      return 0;
+    }
     max_clusters[dev] = n;
   }
-  const int ncl = p.num_tiles < max_clusters[dev] ? p.num_tiles : max_clusters[dev];
+  return max_clusters[dev];
+}
+
+// Launches the CTA-pair kernel; grid = 2 x min(tiles, co-resident clusters).
+template <bool PROMOTE, bool SWAP>
+int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, int dev, cudaStream_t st) {
+  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP>;
+  const int maxc = pair_max_clusters<PROMOTE, SWAP>(dev);
+  if (maxc <= 0) return QI8_EUNSUPPORTED;
+  const int ncl = p.num_tiles < maxc ? p.num_tiles : maxc;
   kern<<<2 * ncl, THREADS, pairk::P_SMEM, st>>>(mapA, mapB, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1252,6 +1281,70 @@ int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs
                 fa.numRegs, pairk::P_SMEM, ncl);
   }
   return QI8_OK;
+}
+
+// Split-K reduction with the plain epilogue: acc = sum of the S int32
+// planes (exact), then the same arithmetic as the GEMM's own epilogue,
+// y = fl(fl(acc) * fl(x_s * w_s)) (+ bias) (GELU) -> out dtype
+// (comfy/quant_ops.py:472-474).  Four consecutive columns per thread.
+__global__ void splitk_finalize_kernel(const int32_t* __restrict__ ws, int S, int64_t plane, int M, int N,
+                                       const float* __restrict__ a_scale, int a_kind, const float* __restrict__ b_scale,
+                                       int b_kind, const void* __restrict__ bias, int bias_dtype, void* out,
+                                       int out_dtype, int64_t ld_out, int act) {
+  const int nq = N >> 2;
+  const int64_t total = (int64_t)M * nq;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / nq), n = (int)(i - (int64_t)m * nq) * 4;
+    const int32_t* src = ws + (int64_t)m * N + n;
+    int4 a = *reinterpret_cast<const int4*>(src);
+    for (int sp = 1; sp < S; ++sp) {
+      const int4 b = *reinterpret_cast<const int4*>(src + sp * plane);
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    const int acc[4] = {a.x, a.y, a.z, a.w};
+    const int64_t o = (int64_t)m * ld_out + n;
+    if (out_dtype == QI8_I32) {
+      *reinterpret_cast<int4*>(static_cast<int32_t*>(out) + o) = a;
+      continue;
+    }
+    const float fr = row_scale(a_scale, a_kind, m);
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      y[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(fr, row_scale(b_scale, b_kind, n + j)));
+      if (bias) y[j] = __fadd_rn(y[j], load_as_f32(bias, bias_dtype, n + j));
+      if (act == QI8_ACT_GELU) y[j] = act_gelu(y[j], out_dtype);
+    }
+    if (out_dtype == QI8_F32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(out) + o) = make_float4(y[0], y[1], y[2], y[3]);
+    } else {
+      uint2 u;
+      if (out_dtype == QI8_BF16) {
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]), h1 = __floats2bfloat162_rn(y[2], y[3]);
+        u = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+      } else {
+        __half2 h0 = __floats2half2_rn(y[0], y[1]), h1 = __floats2half2_rn(y[2], y[3]);
+        u = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+      }
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + o) = u;
+    }
+  }
+}
+
+// K splits of a plain-scale GEMM on the pair kernel: only when its tiles
+// fill at most half of the co-resident CTA pairs and K has >= 8 blocks per
+// split... returns the number of splits (1 = none) and the blocks per split.
+int choose_splits(int64_t Rrows, int64_t Crows, int64_t K, int max_clusters, int* kb_split) {
+  const int KB = (int)((K + BK - 1) / BK);
+  *kb_split = KB;
+  const int64_t tiles = ((Rrows + 255) / 256) * ((Crows + pairk::PBN - 1) / pairk::PBN);
+  if (max_clusters <= 0 || tiles * 2 > max_clusters || KB < 16) return 1;
+  int s = (int)(max_clusters / tiles);
+  if (s > 8) s = 8;
+  if (s > KB / 8) s = KB / 8;
+  if (s < 2) return 1;
+  *kb_split = (KB + s - 1) / s;
+  return (KB + *kb_split - 1) / *kb_split;
 }
 
 }  // namespace
@@ -1266,7 +1359,8 @@ namespace {
 // receives the full [M, N] result at row stride ld_out.
 int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale, int a_kind,
                 const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* const* outs, int n_outs,
-                int out_dtype, int64_t ld_out, int act, void* stream) {
+                int out_dtype, int64_t ld_out, int act, void* stream, void* workspace = nullptr,
+                int64_t workspace_bytes = 0) {
   QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
   QI8_REQUIRE(A && B && outs && n_outs >= 1 && n_outs <= QI8_MAX_PEERS, QI8_EINVAL, "null pointer or bad n_outs");
   for (int d = 0; d < n_outs; ++d) QI8_REQUIRE(outs[d], QI8_EINVAL, "null output pointer %d", d);
@@ -1317,11 +1411,38 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     set_outs(p, outs, n_outs);
     p.act = act;
     p.status = device_status_ptr();
+    p.kb_split = p.KB;
+    p.split_stride = 0;
     CUtensorMap mapA, mapB;
     int rc = make_map(&mapA, Rop, Rrows, K, 128);
     if (rc) return rc;
     rc = make_map(&mapB, Cop, Crows, K, bnp / 2);
     if (rc) return rc;
+    if (!promote && n_outs == 1 && workspace) {
+      // few tiles: split K over more CTA pairs, int32 partial planes, then one reduce + epilogue pass
+      int kb_split = p.KB;
+      const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false>(dev), &kb_split);
+      if (S > 1 && workspace_bytes >= (int64_t)S * M * N * 4 && aligned16(workspace)) {
+        GemmArgs q = p;
+        q.kb_split = kb_split;
+        q.num_tiles = p.num_tiles * S;
+        q.split_stride = M * N;
+        q.ld_out = N;
+        q.out_dtype = QI8_I32;
+        void* ws_out[1] = {workspace};
+        set_outs(q, ws_out, 1);
+        rc = launch_pair<false, false>(mapA, mapB, q, dev, st);
+        if (rc) return rc;
+        const int64_t work = M * (N / 4);
+        int64_t blocks = (work + 255) / 256;
+        const int64_t cap = (int64_t)(sm_count() > 0 ? sm_count() : 148) * 8;
+        if (blocks > cap) blocks = cap;
+        splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const int32_t*>(workspace), S, M * N,
+                                                                 (int)M, (int)N, a_scale, a_kind, b_scale, b_kind,
+                                                                 bias, bias_dtype, outs[0], out_dtype, ld_out, act);
+        return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
+      }
+    }
     if (!promote) return launch_pair<false, false>(mapA, mapB, p, dev, st);
     if (swap) return launch_pair<true, true>(mapA, mapB, p, dev, st);
     return launch_pair<true, false>(mapA, mapB, p, dev, st);
@@ -1379,6 +1500,25 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
   void* outs[1] = {out};
   return gemm_launch(A, B, M, N, K, a_scale, a_kind, b_scale, b_kind, bias, bias_dtype, outs, 1, out_dtype, ld_out,
                      act, stream);
+}
+
+extern "C" int64_t qi8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_kind, int b_kind) {
+  if (!device_ok() || M <= 128 || N <= 0 || K <= 0) return 0;
+  if (a_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_TILE128) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int kb_split = 0;
+  const int S = choose_splits(M, N, K, pair_max_clusters<false, false>(dev), &kb_split);
+  return S > 1 ? (int64_t)S * M * N * 4 : 0;
+}
+
+extern "C" int qi8_gemm_i8_ws(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                              int a_kind, const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* out,
+                              int out_dtype, int64_t ld_out, int act, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  void* outs[1] = {out};
+  return gemm_launch(A, B, M, N, K, a_scale, a_kind, b_scale, b_kind, bias, bias_dtype, outs, 1, out_dtype, ld_out,
+                     act, stream, workspace, workspace_bytes);
 }
 
 extern "C" int qi8_gemm_i8_gather(const int8_t* A, const int8_t* B_local, int64_t M, int64_t n_loc, int64_t K,

@@ -87,6 +87,20 @@ def gemm_cases(run, dev):
         res[f"k2_block_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
         us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, sb, L.QI8_S_ROW, None, torch.bfloat16, out=out))
         res[f"k2_row_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+    # the rotated single linear's GEMM (512 tokens, tensorwise weight scale, fp32 out): split-K vs one pass
+    M, N, K = 512, 4096, 4096
+    a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=dev)
+    sa = torch.rand(M, 1, device=dev) * 0.01
+    s1 = torch.full((), 0.003, device=dev)
+    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    lib = L.load()
+    us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, s1, L.QI8_S_SCALAR, None, torch.float32, out=out))
+    res[f"k2_scalar_splitk_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+    us = run(lambda: L.check(lib.qi8_gemm_i8(L.ptr(a), L.ptr(b), M, N, K, L.ptr(sa), L.QI8_S_ROW, L.ptr(s1),
+                                             L.QI8_S_SCALAR, None, 0, L.ptr(out), L.QI8_F32, N, L.QI8_ACT_NONE,
+                                             L.stream_ptr(dev))))
+    res[f"k2_scalar_onepass_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
     return res
 
 

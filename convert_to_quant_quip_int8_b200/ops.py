@@ -164,10 +164,25 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, a_scale: Optional[torch.Tensor] = 
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     bb = None if bias is None else bias.contiguous()
     lib = L.load()
-    L.check(lib.qi8_gemm_i8(L.ptr(a2), L.ptr(b), M, N, K, L.ptr(a_scale), a_kind, L.ptr(b_scale), b_kind,
-                            L.ptr(bb), L.dtype_code(bb.dtype) if bb is not None else 0, L.ptr(out),
-                            L.dtype_code(out.dtype), out.stride(0), act, L.stream_ptr(a.device)), "qi8_gemm_i8")
+    # small output grids split K (int32 partials in a workspace, identical results)
+    ws_bytes = _gemm_ws_bytes(M, N, K, a_kind, b_kind)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device) if ws_bytes else None
+    L.check(lib.qi8_gemm_i8_ws(L.ptr(a2), L.ptr(b), M, N, K, L.ptr(a_scale), a_kind, L.ptr(b_scale), b_kind,
+                               L.ptr(bb), L.dtype_code(bb.dtype) if bb is not None else 0, L.ptr(out),
+                               L.dtype_code(out.dtype), out.stride(0), act, L.ptr(ws), ws_bytes,
+                               L.stream_ptr(a.device)), "qi8_gemm_i8")
     return out.reshape(*a.shape[:-1], N)
+
+
+_WS_CACHE = {}
+
+
+def _gemm_ws_bytes(M: int, N: int, K: int, a_kind: int, b_kind: int) -> int:
+    key = (torch.cuda.current_device(), M, N, K, a_kind, b_kind)
+    v = _WS_CACHE.get(key)
+    if v is None:
+        v = _WS_CACHE[key] = int(L.load().qi8_gemm_workspace_bytes(M, N, K, a_kind, b_kind))
+    return v
 
 
 def dequant(q: torch.Tensor, scale: torch.Tensor, kind: int, block: int = 128,

@@ -245,6 +245,22 @@ QI8_API int qi8_allgather_cols(const void* y_local, int dtype, int64_t rows, int
 QI8_API int qi8_gather_layout(const void* gathered, int dtype, int world, int64_t rows, int64_t n_loc,
                               void* y_out, int64_t ld_out, void* stream);
 
+/* Device workspace (bytes) with which qi8_gemm_i8_ws splits K over more CTA
+   pairs for this shape: nonzero only for plain (tensor / row / none) scales
+   when the output tiles fill at most half of the device's co-resident CTA
+   pairs (e.g. 512 tokens x 4096 x 4096); 0 = no split.  Needs the device. */
+QI8_API int64_t qi8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_kind, int b_kind);
+
+/* qi8_gemm_i8 with a caller workspace: when workspace_bytes >=
+   qi8_gemm_workspace_bytes(...) the K blocks are split over S CTA-pair tiles
+   that store exact int32 partial sums into the workspace ([S, M, N]), and one
+   reduce pass sums them and applies the epilogue (same arithmetic, so the
+   result is identical to qi8_gemm_i8); otherwise it is qi8_gemm_i8. */
+QI8_API int qi8_gemm_i8_ws(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                           int a_kind, const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* out,
+                           int out_dtype, int64_t ld_out, int act, void* workspace, int64_t workspace_bytes,
+                           void* stream);
+
 /* Column-parallel K2 with the output all-gather fused into the epilogue
    (multi-GPU inference, one process per GPU).  Rank `rank` of `world` holds
    weight rows [rank*n_loc, (rank+1)*n_loc) as B_local [n_loc, K] (scales and
