@@ -88,30 +88,36 @@ struct GemmArgs {
   int b_kind;
   const void* bias;
   int bias_dtype;
-  // Output destinations, each [M, ld_out] from its own base: outs[0] on this
-  // device; outs[1..n_outs) peer-mapped copies (column-parallel gather),
-  // which receive the same tile at the same offset.
-  void* outs[QI8_MAX_PEERS];
-  int n_outs;
+  void* out;
   int out_dtype;
   int64_t ld_out;
   int act;
   unsigned int* status;
+};
+
+// Launch extensions, a separate kernel parameter so that the common
+// single-output kernels keep GemmArgs unchanged.
+struct GemmExt {
   // split-K (plain path of the pair kernel): tile t covers K blocks
   // [s * kb_split, (s + 1) * kb_split) of split s = t / (r_tiles * c_tiles) and
   // stores its raw int32 sums to plane s (split_stride elements apart)
   int kb_split;
   int64_t split_stride;
+  // Output destinations, each [M, ld_out] from its own base: outs[0] == out
+  // on this device; outs[1..n_outs) peer-mapped copies (column-parallel
+  // gather), which receive the same tile at the same offset.
+  int n_outs;
+  void* outs[QI8_MAX_PEERS];
 };
 
 // Calls f(base) for every output destination (static indices, so the
 // parameter struct stays in the constant bank).
 template <typename F>
-__device__ __forceinline__ void for_each_out(const GemmArgs& p, F&& f) {
+__device__ __forceinline__ void for_each_out(const GemmExt& e, F&& f) {
 #pragma unroll
   for (int d = 0; d < QI8_MAX_PEERS; ++d) {
-    if (d >= p.n_outs) break;
-    f(p.outs[d]);
+    if (d >= e.n_outs) break;
+    f(e.outs[d]);
   }
 }
 
@@ -234,8 +240,9 @@ __device__ __forceinline__ float act_gelu(float y, int out_dtype) {
   return gelu_erf(y);
 }
 
-// Stores 32 consecutive fp32 results of row m starting at column n0.
-__device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, const float (&y)[32]) {
+// Multi-destination forms: every outs[d] receives the values.
+__device__ __forceinline__ void store_row32_multi(const GemmArgs& p, const GemmExt& e, int m, int n0,
+                                                  const float (&y)[32]) {
   const int64_t off = (int64_t)m * p.ld_out + n0;
   const bool full = (n0 + 32 <= p.N);
   if (p.out_dtype == QI8_BF16 || p.out_dtype == QI8_F16) {
@@ -257,13 +264,13 @@ __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, co
           }
         }
       }
-      for_each_out(p, [&](void* base) {
+      for_each_out(e, [&](void* base) {
         uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off);
 #pragma unroll
         for (int k = 0; k < 4; ++k) o[k] = u[k];
       });
     } else {
-      for_each_out(p, [&](void* base) {
+      for_each_out(e, [&](void* base) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (n0 + j >= p.N) continue;
@@ -273,7 +280,7 @@ __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, co
       });
     }
   } else {
-    for_each_out(p, [&](void* base) {
+    for_each_out(e, [&](void* base) {
       float* o = static_cast<float*>(base) + off;
       if (full) {
 #pragma unroll
@@ -288,8 +295,8 @@ __device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, co
   }
 }
 
-// Stores 8 consecutive fp32 results of row m starting at column n0 (n0 % 8 == 0).
-__device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, const float (&y)[8]) {
+__device__ __forceinline__ void store_row8_multi(const GemmArgs& p, const GemmExt& e, int m, int n0,
+                                                 const float (&y)[8]) {
   const int64_t off = (int64_t)m * p.ld_out + n0;
   const bool full = (n0 + 8 <= p.N);
   if (p.out_dtype == QI8_BF16 || p.out_dtype == QI8_F16) {
@@ -307,9 +314,9 @@ __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, con
           w[j] = *reinterpret_cast<uint32_t*>(&h);
         }
       }
-      for_each_out(p, [&](void* base) { *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) = u; });
+      for_each_out(e, [&](void* base) { *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) = u; });
     } else {
-      for_each_out(p, [&](void* base) {
+      for_each_out(e, [&](void* base) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (n0 + j >= p.N) continue;
@@ -319,7 +326,7 @@ __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, con
       });
     }
   } else {
-    for_each_out(p, [&](void* base) {
+    for_each_out(e, [&](void* base) {
       float* o = static_cast<float*>(base) + off;
       if (full) {
         reinterpret_cast<float4*>(o)[0] = make_float4(y[0], y[1], y[2], y[3]);
@@ -333,9 +340,114 @@ __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, con
   }
 }
 
+// Stores 32 consecutive fp32 results of row m starting at column n0.
+__device__ __forceinline__ void store_row32(const GemmArgs& p, int m, int n0, const float (&y)[32]) {
+  const int64_t off = (int64_t)m * p.ld_out + n0;
+  const bool full = (n0 + 32 <= p.N);
+  if (p.out_dtype == QI8_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + off;
+    if (full) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 u;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[8 * k + 2 * j], y[8 * k + 2 * j + 1]);
+        reinterpret_cast<uint4*>(o)[k] = u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = __float2bfloat16_rn(y[j]);
+    }
+  } else if (p.out_dtype == QI8_F16) {
+    __half* o = static_cast<__half*>(p.out) + off;
+    if (full) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(y[8 * k + 2 * j], y[8 * k + 2 * j + 1]);
+        reinterpret_cast<uint4*>(o)[k] = u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = __float2half_rn(y[j]);
+    }
+  } else {
+    float* o = static_cast<float*>(p.out) + off;
+    if (full) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        reinterpret_cast<float4*>(o)[k] = make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = y[j];
+    }
+  }
+}
+
+// Stores 8 consecutive fp32 results of row m starting at column n0 (n0 % 8 == 0).
+__device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, const float (&y)[8]) {
+  const int64_t off = (int64_t)m * p.ld_out + n0;
+  const bool full = (n0 + 8 <= p.N);
+  if (p.out_dtype == QI8_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + off;
+    if (full) {
+      uint4 u;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+      *reinterpret_cast<uint4*>(o) = u;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = __float2bfloat16_rn(y[j]);
+    }
+  } else if (p.out_dtype == QI8_F16) {
+    __half* o = static_cast<__half*>(p.out) + off;
+    if (full) {
+      uint4 u;
+      __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+      *reinterpret_cast<uint4*>(o) = u;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = __float2half_rn(y[j]);
+    }
+  } else {
+    float* o = static_cast<float*>(p.out) + off;
+    if (full) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < p.N) o[j] = y[j];
+    }
+  }
+}
+
+template <bool MULTI>
+__device__ __forceinline__ void store_row32_t(const GemmArgs& p, const GemmExt& e, int m, int n0,
+                                              const float (&y)[32]) {
+  if constexpr (MULTI) store_row32_multi(p, e, m, n0, y);
+  else store_row32(p, m, n0, y);
+}
+template <bool MULTI>
+__device__ __forceinline__ void store_row8_t(const GemmArgs& p, const GemmExt& e, int m, int n0, const float (&y)[8]) {
+  if constexpr (MULTI) store_row8_multi(p, e, m, n0, y);
+  else store_row8(p, m, n0, y);
+}
+
 __device__ __forceinline__ void store_row32_i32(const GemmArgs& p, int m, int n0, const uint32_t (&r)[32],
                                                 int64_t plane = 0) {
-  int32_t* o = static_cast<int32_t*>(p.outs[0]) + plane + (int64_t)m * p.ld_out + n0;  // int32: one destination
+  int32_t* o = static_cast<int32_t*>(p.out) + plane + (int64_t)m * p.ld_out + n0;  // int32: one destination
   if (n0 + 32 <= p.N) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) reinterpret_cast<uint4*>(o)[k] = make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
@@ -357,8 +469,9 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
 // SWAP: thread = output feature rr, the 128 values are tokens cc0..cc0+127;
 // stores go through a per-warp 16x32 bf16 transpose tile so each lane writes
 // 32 contiguous bytes.  Otherwise: thread = token rr, values = features.
-template <bool SWAP, bool GELU, int WC = 128>
-__device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&acc)[WC / 2], const float* my_col,
+template <bool SWAP, bool GELU, bool MULTI, int WC = 128>
+__device__ __forceinline__ void finalize_tile(const GemmArgs& p, const GemmExt& e, const float2 (&acc)[WC / 2],
+                                              const float* my_col,
                                               const float* my_bias, float frow, float brow, int rr, int cc0, int cc1,
                                               int R, int C, int warp, int lane, __nv_bfloat16* sxp) {
   // accumulator column j < WC/2 is output column cc0 + j, column j >= WC/2 is cc1 + j - WC/2
@@ -402,12 +515,19 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
         const int f0 = rr - lane + h * 16;  // first of the 16 features this lane stores
         if (tok < C && f0 < R) {
           const uint4* src = reinterpret_cast<const uint4*>(tb + t * 32 + h * 16);
-          const uint4 v0 = src[0], v1 = src[1];
-          for_each_out(p, [&](void* base) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + (int64_t)tok * p.ld_out + f0);
-            dst[0] = v0;
-            dst[1] = v1;
-          });
+          if constexpr (MULTI) {
+            const uint4 v0 = src[0], v1 = src[1];
+            for_each_out(e, [&](void* base) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + (int64_t)tok * p.ld_out + f0);
+              dst[0] = v0;
+              dst[1] = v1;
+            });
+          } else {
+            uint4* dst =
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)tok * p.ld_out + f0);
+            dst[0] = src[0];
+            dst[1] = src[1];
+          }
         }
       } else if (row_ok) {
 #pragma unroll
@@ -418,10 +538,15 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
           if (GELU) y = act_gelu(y, p.out_dtype);
           if (col0 + j < C) {
             const int64_t o = (int64_t)(col0 + j) * p.ld_out + rr;
-            for_each_out(p, [&](void* base) {
-              if (p.out_dtype == QI8_F16) static_cast<__half*>(base)[o] = __float2half_rn(y);
-              else static_cast<float*>(base)[o] = y;
-            });
+            if constexpr (MULTI) {
+              for_each_out(e, [&](void* base) {
+                if (p.out_dtype == QI8_F16) static_cast<__half*>(base)[o] = __float2half_rn(y);
+                else static_cast<float*>(base)[o] = y;
+              });
+            } else {
+              if (p.out_dtype == QI8_F16) static_cast<__half*>(p.out)[o] = __float2half_rn(y);
+              else static_cast<float*>(p.out)[o] = y;
+            }
           }
         }
       }
@@ -446,7 +571,7 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
         y[j] = __fadd_rn(__fmul_rn(__fmul_rn(a, frow), cs[j]), bs[j]);
         if (GELU) y[j] = act_gelu(y[j], p.out_dtype);
       }
-      store_row8(p, rr, n0, y);
+      store_row8_t<MULTI>(p, e, rr, n0, y);
     }
   }
 }
@@ -455,10 +580,10 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const float2 (&
 // and the activation tile the B operand (TMEM columns = tokens).  Used when
 // the weight scale varies per (row, K block) and the activation scale does
 // not, so that every epilogue thread promotes with one scalar per K block.
-template <bool PROMOTE, bool SWAP>
+template <bool PROMOTE, bool SWAP, bool MULTI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs p) {
+                   const GemmArgs p, const GemmExt e) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -729,9 +854,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // warp enters together; lanes whose row is out of range store nothing
         if (cols_ok && (SWAP || row_ok)) {
           if (p.act == QI8_ACT_GELU)
-            finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
+            finalize_tile<SWAP, true, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
           else
-            finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
+            finalize_tile<SWAP, false, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
         }
       } else {
         const int m = rr;
@@ -771,7 +896,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
                 if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
               }
-              store_row32(p, m, n0, y);
+              store_row32_t<MULTI>(p, e, m, n0, y);
             }
           }
         }
@@ -871,10 +996,10 @@ __device__ __forceinline__ void commit_pair(uint32_t bar, uint16_t mask) {
 
 // One accumulation unit per K block (block-scaled) or per tile (plain), in
 // TMEM buffer (unit % 2); each epilogue warp drains 32 lanes x 128 columns.
-template <bool PROMOTE, bool SWAP>
+template <bool PROMOTE, bool SWAP, bool MULTI, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs p) {
+                     const GemmArgs p, const GemmExt e) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -939,8 +1064,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
-          const int rc = tile % rc_tiles, kb_lo = (tile / rc_tiles) * p.kb_split;
-          const int kb_hi = kb_lo + p.kb_split < KB ? kb_lo + p.kb_split : KB;
+          int rc = tile, kb_lo = 0, kb_hi = KB;
+          if constexpr (SPLIT) {
+            rc = tile % rc_tiles;
+            kb_lo = (tile / rc_tiles) * e.kb_split;
+            kb_hi = kb_lo + e.kb_split < KB ? kb_lo + e.kb_split : KB;
+          }
           const int r0 = (rc % r_ptiles) * 256 + (int)rank * 128;
           const int c0 = (rc / r_ptiles) * PBN + (int)rank * B_HALF;
           for (int kb = kb_lo; kb < kb_hi; ++kb) {
@@ -975,8 +1104,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             const uint32_t d = tmem_base + (uint32_t)(buf * PBN);
-            const int kb_lo = (tile / rc_tiles) * p.kb_split;
-            const int kb_n = PROMOTE ? 1 : (kb_lo + p.kb_split < KB ? p.kb_split : KB - kb_lo);
+            int kb_n = PROMOTE ? 1 : KB;
+            if constexpr (SPLIT) {
+              const int kb_lo = (tile / rc_tiles) * e.kb_split;
+              kb_n = kb_lo + e.kb_split < KB ? e.kb_split : KB - kb_lo;
+            }
             for (int kb = 0; kb < kb_n; ++kb) {
               if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, ST_GEMM_MMA, WAIT_LIMIT_NS)) {
                 ok = false;
@@ -1018,8 +1150,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int au = 0;
     bool ok = true;
     for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
-      const int rc = tile % rc_tiles;
-      const int64_t plane = (int64_t)(tile / rc_tiles) * p.split_stride;
+      int rc = tile;
+      int64_t plane = 0;
+      if constexpr (SPLIT) {
+        rc = tile % rc_tiles;
+        plane = (int64_t)(tile / rc_tiles) * e.split_stride;
+      }
       const int rr = (rc % r_ptiles) * 256 + (int)rank * 128 + quad * 32 + lane;
       const int c0 = (rc / r_ptiles) * PBN;
       // this warp's 128 accumulator columns (output columns cc0 .. cc0 + 127)
@@ -1125,9 +1261,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (!ok) break;
         if (cols_ok && (SWAP || row_ok)) {
           if (p.act == QI8_ACT_GELU)
-            finalize_tile<SWAP, true>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
+            finalize_tile<SWAP, true, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
           else
-            finalize_tile<SWAP, false>(p, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
+            finalize_tile<SWAP, false, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
         }
       } else {
         const int buf = au & 1;
@@ -1164,7 +1300,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
                 if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
               }
-              store_row32(p, rr, n0, y);
+              store_row32_t<MULTI>(p, e, rr, n0, y);
             }
           }
         }
@@ -1216,18 +1352,19 @@ int make_map(CUtensorMap* map, const int8_t* ptr, int64_t rows, int64_t K, uint3
   return QI8_OK;
 }
 
-bool g_attr_set[3][64];
+bool g_attr_set[6][64];
 
-void set_outs(GemmArgs& p, void* const* outs, int n_outs) {
-  for (int d = 0; d < QI8_MAX_PEERS; ++d) p.outs[d] = d < n_outs ? outs[d] : nullptr;
-  p.n_outs = n_outs;
+void set_outs(GemmArgs& p, GemmExt& e, void* const* outs, int n_outs) {
+  for (int d = 0; d < QI8_MAX_PEERS; ++d) e.outs[d] = d < n_outs ? outs[d] : nullptr;
+  e.n_outs = n_outs;
+  p.out = outs[0];
 }
 
 // Co-resident CTA pairs of the pair kernel on device `dev` (queried once;
 // 0 with the error set when the kernel cannot run there).
-template <bool PROMOTE, bool SWAP>
+template <bool PROMOTE, bool SWAP, bool MULTI, bool SPLIT>
 int pair_max_clusters(int dev) {
-  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP>;
+  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP, MULTI, SPLIT>;
   static int max_clusters[64];
   if (dev < 0 || dev >= 64) dev = 0;
   if (max_clusters[dev] == 0) {
@@ -1266,18 +1403,19 @@ int pair_max_clusters(int dev) {
 }
 
 // Launches the CTA-pair kernel; grid = 2 x min(tiles, co-resident clusters).
-template <bool PROMOTE, bool SWAP>
-int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, int dev, cudaStream_t st) {
-  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP>;
-  const int maxc = pair_max_clusters<PROMOTE, SWAP>(dev);
+template <bool PROMOTE, bool SWAP, bool MULTI, bool SPLIT = false>
+int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& p, const GemmExt& e, int dev,
+                cudaStream_t st) {
+  auto kern = pairk::gemm_pair_kernel<PROMOTE, SWAP, MULTI, SPLIT>;
+  const int maxc = pair_max_clusters<PROMOTE, SWAP, MULTI, SPLIT>(dev);
   if (maxc <= 0) return QI8_EUNSUPPORTED;
   const int ncl = p.num_tiles < maxc ? p.num_tiles : maxc;
-  kern<<<2 * ncl, THREADS, pairk::P_SMEM, st>>>(mapA, mapB, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
+  kern<<<2 * ncl, THREADS, pairk::P_SMEM, st>>>(mapA, mapB, p, e);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, kern);
-    return fail(QI8_ECUDA, "gemm_pair_kernel launch: %s (regs=%d smem=%d clusters=%d)", cudaGetErrorString(e),
+    return fail(QI8_ECUDA, "gemm_pair_kernel launch: %s (regs=%d smem=%d clusters=%d)", cudaGetErrorString(err),
                 fa.numRegs, pairk::P_SMEM, ncl);
   }
   return QI8_OK;
@@ -1408,11 +1546,12 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     p.num_tiles = p.r_tiles * p.c_tiles;
     p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
     p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
-    set_outs(p, outs, n_outs);
+    GemmExt e{};
+    set_outs(p, e, outs, n_outs);
     p.act = act;
     p.status = device_status_ptr();
-    p.kb_split = p.KB;
-    p.split_stride = 0;
+    e.kb_split = p.KB;
+    e.split_stride = 0;
     CUtensorMap mapA, mapB;
     int rc = make_map(&mapA, Rop, Rrows, K, 128);
     if (rc) return rc;
@@ -1421,17 +1560,18 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     if (!promote && n_outs == 1 && workspace) {
       // few tiles: split K over more CTA pairs, int32 partial planes, then one reduce + epilogue pass
       int kb_split = p.KB;
-      const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false>(dev), &kb_split);
+      const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
       if (S > 1 && workspace_bytes >= (int64_t)S * M * N * 4 && aligned16(workspace)) {
         GemmArgs q = p;
-        q.kb_split = kb_split;
+        GemmExt qe = e;
+        qe.kb_split = kb_split;
         q.num_tiles = p.num_tiles * S;
-        q.split_stride = M * N;
+        qe.split_stride = M * N;
         q.ld_out = N;
         q.out_dtype = QI8_I32;
         void* ws_out[1] = {workspace};
-        set_outs(q, ws_out, 1);
-        rc = launch_pair<false, false>(mapA, mapB, q, dev, st);
+        set_outs(q, qe, ws_out, 1);
+        rc = launch_pair<false, false, false, true>(mapA, mapB, q, qe, dev, st);
         if (rc) return rc;
         const int64_t work = M * (N / 4);
         int64_t blocks = (work + 255) / 256;
@@ -1443,9 +1583,14 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
         return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
       }
     }
-    if (!promote) return launch_pair<false, false>(mapA, mapB, p, dev, st);
-    if (swap) return launch_pair<true, true>(mapA, mapB, p, dev, st);
-    return launch_pair<true, false>(mapA, mapB, p, dev, st);
+    if (n_outs > 1) {
+      if (!promote) return launch_pair<false, false, true>(mapA, mapB, p, e, dev, st);
+      if (swap) return launch_pair<true, true, true>(mapA, mapB, p, e, dev, st);
+      return launch_pair<true, false, true>(mapA, mapB, p, e, dev, st);
+    }
+    if (!promote) return launch_pair<false, false, false>(mapA, mapB, p, e, dev, st);
+    if (swap) return launch_pair<true, true, false>(mapA, mapB, p, e, dev, st);
+    return launch_pair<true, false, false>(mapA, mapB, p, e, dev, st);
   }
   CUtensorMap mapA, mapB;
   int rc = make_map(&mapA, Rop, Rrows, K, BM);
@@ -1460,12 +1605,18 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   p.num_tiles = p.r_tiles * p.c_tiles;
   p.a_scale = a_scale; p.a_kind = a_kind; p.b_scale = b_scale; p.b_kind = b_kind;
   p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
-    set_outs(p, outs, n_outs);
+  GemmExt e{};
+  set_outs(p, e, outs, n_outs);
+  e.kb_split = p.KB;
   p.act = act;
   p.status = device_status_ptr();
 
-  auto kern = !promote ? gemm_i8_kernel<false, false> : (swap ? gemm_i8_kernel<true, true> : gemm_i8_kernel<true, false>);
-  const int variant = !promote ? 0 : (swap ? 2 : 1);
+  auto kern = n_outs > 1
+                  ? (!promote ? gemm_i8_kernel<false, false, true>
+                              : (swap ? gemm_i8_kernel<true, true, true> : gemm_i8_kernel<true, false, true>))
+                  : (!promote ? gemm_i8_kernel<false, false, false>
+                              : (swap ? gemm_i8_kernel<true, true, false> : gemm_i8_kernel<true, false, false>));
+  const int variant = (!promote ? 0 : (swap ? 2 : 1)) + (n_outs > 1 ? 3 : 0);
   if (dev < 64 && !g_attr_set[variant][dev]) {
     QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     if (promote) {
@@ -1480,13 +1631,13 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   }
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-  kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mapA, mapB, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
+  kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mapA, mapB, p, e);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, kern);
     return fail(QI8_ECUDA, "gemm_i8_kernel launch: %s (regs=%d maxThreads=%d local=%zu smem=%d grid=%d)",
-                cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes, SMEM_BYTES, grid);
+                cudaGetErrorString(err), fa.numRegs, fa.maxThreadsPerBlock, fa.localSizeBytes, SMEM_BYTES, grid);
   }
   return QI8_OK;
 }
@@ -1508,7 +1659,7 @@ extern "C" int64_t qi8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   int kb_split = 0;
-  const int S = choose_splits(M, N, K, pair_max_clusters<false, false>(dev), &kb_split);
+  const int S = choose_splits(M, N, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
   return S > 1 ? (int64_t)S * M * N * 4 : 0;
 }
 
