@@ -12,6 +12,8 @@
 #include <cstdint>
 #include <cmath>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "fwht_row.cuh"
 
@@ -684,10 +686,53 @@ __device__ __forceinline__ float2 magic_q(float2 v, float rcp) {
   return make_float2(__fadd_rn(__fmul_rn(v.x, rcp), RINT_MAGIC), __fadd_rn(__fmul_rn(v.y, rcp), RINT_MAGIC));
 }
 
+// GELU of a pair of T values, rounded to T: gelu_erf on each,
+// (0.5 x) * (1 + erf(x / sqrt 2)) with separately rounded products and sum.
+template <typename T>
+__device__ __forceinline__ uint32_t gelu2(uint32_t w) {
+  const float2 f = Pack<T>::f2(w);
+  const float2 tt = __fmul2_rn(f, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
+  const float2 e = make_float2(erff(tt.x), erff(tt.y));
+  const float2 g = __fmul2_rn(__fmul2_rn(f, make_float2(0.5f, 0.5f)), __fadd2_rn(make_float2(1.0f, 1.0f), e));
+  return Pack<T>::from_f2(g.x, g.y);
+}
+
+// GELU table for bf16 inputs: a bf16 value has 7 mantissa bits, so the
+// binades 2^-16 <= |x| < 16 hold 2 x 20 x 128 values.  Each CTA fills the
+// table with gelu2 itself, so a lookup returns exactly what gelu2 computes;
+// inputs outside the range (zeros, tiny, |x| >= 16, inf/nan) take gelu2.
+constexpr int GT_ELO = 127 - 16, GT_NE = 20;
+constexpr uint32_t GT_HALF = GT_NE * 128, GT_BASE = GT_ELO * 128;
+
+__device__ __forceinline__ void gelu_table_fill(uint32_t* tab) {
+  for (uint32_t i = threadIdx.x; i < GT_HALF; i += blockDim.x) {  // word i = entries 2i, 2i+1
+    const uint32_t k = 2 * i, s = k >= GT_HALF ? 1u : 0u, r = k - s * GT_HALF;
+    const uint32_t b0 = (s << 15) | (GT_BASE + r);
+    tab[i] = gelu2<__nv_bfloat16>(b0 | ((b0 + 1) << 16));
+  }
+}
+
+__device__ __forceinline__ uint32_t gelu2_lut(uint32_t w, const uint16_t* tab) {
+  const uint32_t t0 = (w & 0x7FFFu) - GT_BASE, t1 = ((w >> 16) & 0x7FFFu) - GT_BASE;
+  if (t0 < GT_HALF && t1 < GT_HALF) {
+    const uint32_t lo = tab[t0 + ((w & 0x8000u) ? GT_HALF : 0u)];
+    const uint32_t hi = tab[t1 + ((w & 0x80000000u) ? GT_HALF : 0u)];
+    return lo | (hi << 16);
+  }
+  return gelu2<__nv_bfloat16>(w);
+}
+
 template <typename T, int CPL, bool GELU>
 __global__ void __launch_bounds__(256, 3) token_rows_kernel(QArgs a, int rows, int W) {
   __shared__ float red[2][8];
   constexpr int EPC = Pack<T>::EPC;
+  constexpr bool LUT = GELU && std::is_same<T, __nv_bfloat16>::value;
+  __shared__ uint32_t gtab_w[LUT ? GT_HALF : 1];
+  if constexpr (LUT) {
+    gelu_table_fill(gtab_w);
+    __syncthreads();
+  }
+  const uint16_t* gtab = reinterpret_cast<const uint16_t*>(gtab_w);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rpb = 8 / W, wr = warp % W, rsub = warp / W;
   const int nc = a.n / EPC;
@@ -711,15 +756,8 @@ __global__ void __launch_bounds__(256, 3) token_rows_kernel(QArgs a, int rows, i
         uint32_t* w = reinterpret_cast<uint32_t*>(&x[i]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if constexpr (GELU) {
-            // gelu_erf on a pair: (0.5 x) * (1 + erf(x / sqrt 2)), the same
-            // separately rounded products and sum as the scalar form
-            const float2 f = Pack<T>::f2(w[j]);
-            const float2 tt = __fmul2_rn(f, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
-            const float2 e = make_float2(erff(tt.x), erff(tt.y));
-            const float2 g = __fmul2_rn(__fmul2_rn(f, make_float2(0.5f, 0.5f)), __fadd2_rn(make_float2(1.0f, 1.0f), e));
-            w[j] = Pack<T>::from_f2(g.x, g.y);
-          }
+          if constexpr (LUT) w[j] = gelu2_lut(w[j], gtab);
+          else if constexpr (GELU) w[j] = gelu2<T>(w[j]);
           m = Pack<T>::absmax2(m, w[j]);
         }
       }

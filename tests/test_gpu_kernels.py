@@ -148,6 +148,22 @@ def test_quant_rows_gelu_equals_torch_gelu_then_quant(n):
     assert torch.equal(q, q2) and torch.equal(s, s2)
 
 
+def test_quant_rows_gelu_every_bf16_value():
+    # one finite bf16 value per row (the rest zeros): the row scale exposes
+    # GELU of that value, so every bf16 input -- table range and outside it --
+    # is checked against torch's bf16 F.gelu
+    bits = torch.arange(65536, dtype=torch.int32)
+    bits = bits[((bits >> 7) & 0xFF) != 0xFF].to(torch.int16)
+    v = bits.view(torch.bfloat16)
+    h = torch.zeros(v.numel(), 16, dtype=torch.bfloat16)
+    h[:, 0] = v
+    h[:, 9] = v
+    h = h.to(dev())
+    q, s = ops.quant_rows(h, L.QI8_Q_TOKEN | L.QI8_Q_GELU)
+    q2, s2 = ops.quant_rows(torch.nn.functional.gelu(h), L.QI8_Q_TOKEN)
+    assert torch.equal(q, q2) and torch.equal(s, s2)
+
+
 def test_quant_rows_block_golden(golden):
     g = golden("triton_quant.npz")
     q, s = ops.quant_rows(bf16_cu(g["x_bf16"]), mode=L.QI8_Q_BLOCK)
