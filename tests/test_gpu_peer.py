@@ -91,7 +91,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, results):
     import datetime
     import torch.distributed as dist
     try:
@@ -107,19 +107,19 @@ def _rank_main(rank, world, port, q):
                for _ in range(4)]
         ok = True
         for req in (L.QI8_REQ_ROW, L.QI8_REQ_BLOCK):
-            q, s = ops.requant_weight(w, req)
-            ref = sharding.ColumnShardedW8A8Linear(q, s, bias, rank=0, world=1)
+            wq, wsc = ops.requant_weight(w, req)
+            ref = sharding.ColumnShardedW8A8Linear(wq, wsc, bias, rank=0, world=1)
             ws = sharding.PeerWorkspace(T * N * 2, world, rank, n_buffers=2)
-            lin = sharding.ColumnShardedW8A8Linear(q, s, bias, rank=rank, world=world, peer=ws)
+            lin = sharding.ColumnShardedW8A8Linear(wq, wsc, bias, rank=rank, world=world, peer=ws)
             outs = [lin(x).clone() for x in xs_]  # four calls: both buffers reused
             torch.cuda.synchronize()
             ops.device_status()
             ok = ok and all(torch.equal(o, ref(x)) for o, x in zip(outs, xs_))
             ws.close()
-        q.put((rank, ok))
+        results.put((rank, ok))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent
-        q.put((rank, repr(e)))
+        results.put((rank, repr(e)))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
@@ -132,7 +132,7 @@ def test_fused_gather_two_ranks_equals_unsharded():
         p.start()
     res = {}
     for _ in range(2):
-        rk, v = q.get(timeout=240)
+        rk, v = q.get(timeout=150)
         res[rk] = v
     for p in procs:
         p.join(timeout=60)
