@@ -433,6 +433,44 @@ __device__ __forceinline__ void store_row8(const GemmArgs& p, int m, int n0, con
   }
 }
 
+// Multi-destination store of a warp's 32 rows x 32 columns (16-bit output):
+// each lane packs its row into the warp's 2 KB tile (16-byte chunks XOR-
+// swizzled, conflict-free), then lanes 4r..4r+3 write row r's 64 contiguous
+// bytes to every destination -- wide row segments instead of one 16-byte
+// piece per row, which is what NVLink stores need.  Warp-collective.
+__device__ __forceinline__ void store_tile32_multi(const GemmArgs& p, const GemmExt& e, uint4* tile, int row0, int R,
+                                                   int n0, const float (&y)[32], int lane) {
+  const bool bf = p.out_dtype == QI8_BF16;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = y[8 * k + 2 * j], b = y[8 * k + 2 * j + 1];
+      if (bf) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(a, b);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    tile[lane * 4 + (k ^ ((lane >> 1) & 3))] = u;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2), k = lane & 3;
+    const uint4 v = tile[r * 4 + (k ^ ((r >> 1) & 3))];
+    if (row0 + r < R) {
+      const int64_t off = (int64_t)(row0 + r) * p.ld_out + n0 + k * 8;
+      for_each_out(e, [&](void* base) { *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) = v; });
+    }
+  }
+  __syncwarp();
+}
+
 template <bool MULTI>
 __device__ __forceinline__ void store_row32_t(const GemmArgs& p, const GemmExt& e, int m, int n0,
                                               const float (&y)[32]) {
@@ -1288,6 +1326,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           for (int c = 0; c < 2; ++c) {
             const int cc = rnd * 64 + c * 32;
             const int n0 = cc0 + cc;
+            if constexpr (MULTI) {
+              // peer destinations: the warp's 32 x 32 tile goes through shared
+              // memory so that each store writes 64 contiguous bytes of a row
+              if (n0 < p.N && n0 + 32 <= p.N && p.out_dtype != QI8_F32) {  // warp-uniform
+                float y[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(frow, my_col[cc + j]));
+                  if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
+                  if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
+                }
+                store_tile32_multi(p, e, reinterpret_cast<uint4*>(sxp + warp * (2 * 16 * 32)), rr - lane, R, n0,
+                                   y, lane);
+                continue;
+              }
+            }
             if (!row_ok || n0 >= p.N) continue;
             if (p.out_dtype == QI8_I32) {
               store_row32_i32(p, rr, n0, r[c], plane);
