@@ -67,9 +67,10 @@ def parse():
                     help="dit_mlp: the headline DiT MLP pair; quip_linear: one rotated W8A8 linear "
                          "(K1 rotate -> K2 -> K3); conversion: the 304-tensor QuIP conversion sweep; "
                          "flux_stack / t5_stack: the 228-linear Flux-shaped / 168-linear T5-XXL stacks")
-    ap.add_argument("--shard", default="replica", choices=["replica", "columns"],
+    ap.add_argument("--shard", default="replica", choices=["replica", "columns", "tokens"],
                     help="stacks on N>1 GPUs: replica = one batch per rank (weak scaling); columns = every "
-                         "linear column-sharded with overlapped NCCL all-gathers (strong scaling)")
+                         "linear column-sharded with its output gathered on every rank; tokens = full weights, "
+                         "each rank 1/N of the tokens (both strong scaling)")
     ap.add_argument("--chunks", type=int, default=4, help="token chunks per column-sharded linear (nccl gather)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="column-sharded output gather: peer = fused into the GEMM epilogue (stores into every "
@@ -461,7 +462,7 @@ def main_stack(args):
     ms_step = ms / args.steps
     tokens = cfg["tokens"]
     value = (world if shard == "replica" else 1) * tokens * args.steps / (ms / 1e3)
-    fwd_ops = ops_per_forward(st.specs)
+    fwd_ops = ops_per_forward(st.specs) * (world if shard == "tokens" else 1)
 
     # GEMM kernel time: one eager forward with CUDA events around every linear's GEMM launches
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in st.specs]
@@ -536,7 +537,9 @@ def main_stack(args):
                    "parallelism": ((f"column-sharded x{world}, output gather fused into the GEMM epilogue "
                                     "(peer stores over NVLink + peer barrier)" if args.gather == "peer" else
                                     f"column-sharded x{world}, {args.chunks} token chunks, NCCL all-gather")
-                                   if shard == "columns" else (f"replicas x{world}" if world > 1 else "single")),
+                                   if shard == "columns" else
+                                   (f"token split x{world} (full weights per rank, no exchange)" if shard == "tokens"
+                                    else (f"replicas x{world}" if world > 1 else "single"))),
                    "graph": "one CUDA graph per forward",
                    "l2": "inputs larger than L2: every forward streams 8.6 GB (flux) / 4.6 GB (t5) of int8 weights"},
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),

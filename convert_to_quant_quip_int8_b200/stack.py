@@ -23,6 +23,8 @@ fused GELU.  Attention, norms and modulation are outside the stack.
 
 Multi-GPU (one process per GPU):
 * ``replica``: every rank runs the whole stack on its own batch.
+* ``tokens``: every rank holds all weights and runs every linear on its 1/G
+  of the forward's tokens -- no exchange inside the linear stack.
 * ``columns``: every linear is column-sharded -- rank r holds weight rows
   ``[r N/G, (r+1) N/G)`` -- and K1 runs on every rank.  ``gather="peer"``:
   the GEMM epilogue stores each tile into every rank's peer-mapped output
@@ -94,6 +96,11 @@ class LinearStack:
         cfg = STACKS[name]
         self.name, self.cfg, self.device = name, cfg, device
         self.specs = cfg["specs"]() if specs is None else list(specs)
+        if shard == "tokens" and world > 1:
+            # token split: full weights on every rank, each rank its 1/G of every linear's tokens
+            for sp in self.specs:
+                assert sp.tokens % world == 0, f"{sp.name}: {sp.tokens} tokens do not split over {world} ranks"
+            self.specs = [LinearSpec(sp.name, sp.tokens // world, sp.k, sp.n, sp.src, sp.gelu) for sp in self.specs]
         self.rank, self.world, self.group = rank, world, group
         self.sharded = shard == "columns" and world > 1
         self.chunks = chunks
