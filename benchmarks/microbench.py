@@ -1,9 +1,9 @@
 """Kernel micro-benchmarks of the QuIP W8A8 path (one GPU).
 
-    python -m convert_to_quant_quip_int8_b200.microbench rotate   # K1 rotate+quant, K3 unrotate
-    python -m convert_to_quant_quip_int8_b200.microbench quant    # K1 per-token quant (+ fused GELU)
-    python -m convert_to_quant_quip_int8_b200.microbench gemm     # K2 block-scaled / per-row GEMM
-    python -m convert_to_quant_quip_int8_b200.microbench convert  # K4 QuIP conversion
+    python benchmarks/microbench.py rotate   # K1 rotate+quant, K3 unrotate
+    python benchmarks/microbench.py quant    # K1 per-token quant (+ fused GELU)
+    python benchmarks/microbench.py gemm     # K2 block-scaled / per-row GEMM
+    python benchmarks/microbench.py convert  # K4 QuIP conversion
 
 Each case is timed with CUDA events around one launch, median of ``--iters``
 launches, with a 256 MB buffer rewritten between launches so every launch
@@ -16,11 +16,15 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import torch
 
-from . import _lib as L
-from . import ops
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from convert_to_quant_quip_int8_b200 import _lib as L  # noqa: E402
+from convert_to_quant_quip_int8_b200 import ops  # noqa: E402
 
 
 def _timer(flush: torch.Tensor, iters: int, profile: bool):

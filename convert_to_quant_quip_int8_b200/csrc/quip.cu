@@ -17,6 +17,7 @@
 // A column pass holds up to 512 rows x 32 columns in shared memory and
 // performs the butterfly stages of a contiguous range of row-index bits;
 // ranges run in ascending order, so the stage order equals the reference's.
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 
@@ -312,19 +313,22 @@ constexpr int64_t NOALLOC_BYTES = NOALLOC_MAX_ELEMS * 4 + 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
 
 // Device address of g_noalloc_scratch, looked up once per device with that
-// device current (host code only sees a stand-in for the symbol).
-void* g_noalloc_ptr[64];
+// device current (host code only sees a stand-in for the symbol).  Host
+// threads may make their first call on a device concurrently, so the cache
+// entries are atomics; every thread that misses stores the same address.
+// The cached address is not refreshed after cudaDeviceReset.
+std::atomic<void*> g_noalloc_ptr[64];
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   QI8_CUDA(cudaGetDevice(&dev));
   QI8_REQUIRE(dev >= 0 && dev < 64, QI8_EUNSUPPORTED, "device ordinal %d out of range", dev);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
+  void* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
     QI8_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = p;
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return QI8_OK;
 }
 

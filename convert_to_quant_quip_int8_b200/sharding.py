@@ -194,8 +194,12 @@ class PeerWorkspace:
         return self._arrays[j]
 
     def next_buffer(self) -> int:
-        """Alternates between the buffers: an output stays valid until the
-        call after next (two calls per buffer pair)."""
+        """Alternates between the buffers.  With one rank an output stays
+        valid until the call after next.  With several ranks it is valid only
+        until the next call on this workspace is enqueued: once this rank's
+        next peer barrier completes, a peer may start the call after next and
+        store into the buffer again, so any read of an output must be enqueued
+        on this rank's stream before its next call."""
         j = self._next
         self._next = (self._next + 1) % len(self.bufs)
         return j
@@ -297,7 +301,8 @@ class ColumnShardedW8A8Linear:
         T = x2.shape[0]
         xq, xs = ops.quant_rows(x2, L.QI8_Q_TOKEN)
         if self.peer is not None:
-            # fused gather: the output is a view of a peer buffer, valid until the call after next
+            # fused gather: the output is a view of a peer buffer; with several ranks it is valid only
+            # until the next call on this workspace is enqueued (see PeerWorkspace.next_buffer)
             y = gemm_gather(xq, xs, self.w, self.s, self.kind, self.bias, self.peer, self.peer.next_buffer(),
                             self.n_loc * self.world, x.dtype)
         elif self.chunks == 1:

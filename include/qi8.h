@@ -200,7 +200,8 @@ QI8_API int qi8_quip_convert(const void* w, int w_dtype, int64_t M, int64_t N, c
    that loads it until exit; M_pad * N_pad must be <= 2^24 (e.g. 4096 x 4096),
    larger weights are rejected with QI8_ESHAPE.  Nothing is allocated or freed.
    The first call on a device looks up the array's device address (issue it
-   before any stream capture).  All calls share the one array: calls that
+   before any stream capture); the address is cached for the process, so do
+   not use this entry point on a device after cudaDeviceReset.  All calls share the one array: calls that
    overlap on the GPU (different streams, or threads sharing a device) race
    and must be serialized by the caller.  Arguments and results as
    qi8_quip_convert. */

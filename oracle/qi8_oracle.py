@@ -267,9 +267,13 @@ def int8_gemm_block(a: np.ndarray, a_s: np.ndarray, b: np.ndarray, b_s: np.ndarr
     a_s = np.asarray(a_s, dtype=np.float32).reshape(M, -1)
     b_s = np.asarray(b_s, dtype=np.float32).reshape(-1, KB)
     acc = np.zeros((M, N), dtype=np.float32)
+    a32 = np.asarray(a, dtype=np.float32)
+    b32 = np.asarray(b, dtype=np.float32)
     for kb in range(KB):
         sl = slice(kb * block_size, (kb + 1) * block_size)
-        part = int_mm(a[:, sl], b[:, sl]).astype(np.float32)
+        # the int32 partial of one K block: every partial sum is an integer of
+        # magnitude <= 128*128*block_size <= 2**24, exact in fp32 in any order
+        part = a32[:, sl] @ b32[:, sl].T
         sa = a_s[:, kb if a_s.shape[1] > 1 else 0][:, None]
         if b_layout == "row":
             sb = b_s[:, kb][None, :]

@@ -1,8 +1,8 @@
 """Generate the golden vectors under ``tests/golden/`` by running the reference.
 
 This script imports the reference package (ThunderFun/convert_to_quant_QuIP_INT8,
-``convert_to_quant`` v0.8.2) from a checkout given by ``--ref`` (default: the
-read-only mount used when the fixtures were made) and executes its own code on
+``convert_to_quant`` v0.8.2) from a checkout given by ``--ref`` (or the
+``QI8_REFERENCE_PATH`` environment variable) and executes its own code on
 CPU, on seeded inputs:
 
 * the torch CPU path (``utils/hadamard.py``, ``utils/float_utils.py``,
@@ -13,7 +13,7 @@ CPU, on seeded inputs:
 
 The fixtures are small ``.npz`` files (bf16 stored as uint16 bit patterns).
 They are committed; tests only read them, so nothing at test time needs the
-reference.  Re-run with ``python tests/golden/make_golden.py``.
+reference.  Re-run with ``python tests/golden/make_golden.py --ref <checkout>``.
 """
 
 import argparse
@@ -55,7 +55,10 @@ def save(name: str, **arrs):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QI8_REFERENCE_PATH"),
+                    required="QI8_REFERENCE_PATH" not in os.environ,
+                    help="checkout of convert_to_quant (the directory holding the convert_to_quant package); "
+                         "defaults to $QI8_REFERENCE_PATH")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
 

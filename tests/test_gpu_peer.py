@@ -122,6 +122,41 @@ def _rank_main(rank, world, port, results):
         results.put((rank, repr(e)))
 
 
+def test_peer_barrier_wait_expires_and_reports():
+    """The barrier's bounded wait runs out when a peer never arrives: rank 0
+    of a two-rank barrier whose rank-1 flag block is a local buffer nothing
+    writes.  The kernel gives up after its 2 s limit and returns, the status
+    word reports the expiry, the next barrier arrives without waiting, and
+    the context stays usable."""
+    import time
+    ops.device_status(reset=True)
+    mine = torch.zeros(L.QI8_MAX_PEERS + 1, dtype=torch.int32, device="cuda")
+    absent = torch.zeros(L.QI8_MAX_PEERS + 1, dtype=torch.int32, device="cuda")
+    flags = (ctypes.c_void_p * 2)(mine.data_ptr(), absent.data_ptr())
+    lib = L.load()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    L.check(lib.qi8_peer_barrier(flags, 2, 0, L.stream_ptr()), "qi8_peer_barrier")
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert 1.5 < waited < 30.0, f"barrier returned after {waited:.2f} s"
+    # this rank's arrival went into slot 0 of both blocks; its completed-barrier count is 1
+    assert absent[0].item() == 1 and mine[0].item() == 1 and mine[L.QI8_MAX_PEERS].item() == 1
+    # after an expiry later barriers arrive but do not wait
+    t0 = time.perf_counter()
+    L.check(lib.qi8_peer_barrier(flags, 2, 0, L.stream_ptr()), "qi8_peer_barrier")
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    assert absent[0].item() == 2 and mine[L.QI8_MAX_PEERS].item() == 2
+    with pytest.raises(L.QI8Error, match="expired"):
+        ops.device_status(reset=True)
+    ops.device_status(reset=True)  # the bit was cleared by the read above
+    # the context is still usable: a GEMM runs and is correct
+    a = torch.ones(64, 128, dtype=torch.int8, device="cuda")
+    c = ops.gemm_i8(a, a[:32].contiguous(), out_dtype=torch.int32)
+    assert bool((c == 128).all())
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_fused_gather_two_ranks_equals_unsharded():
     ctx = mp.get_context("spawn")
