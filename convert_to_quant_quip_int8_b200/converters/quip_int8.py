@@ -14,8 +14,15 @@ identity Hessian -- then the inverse rotation (:1452, 1489-1506) and either
 reference converter constructed with ``actorder=False,
 use_diagonal_rescaling=False, use_random_permutation=False`` and ``H=None``.
 
-Outside this path (raise ``NotImplementedError``): a calibrated Hessian
-(LDLQ error feedback), diagonal rescaling, random permutation, act-order,
+The constructor keeps the reference's defaults (:33, :50, :52: act-order,
+diagonal rescaling and random permutation all on).  With those on, the
+reference's LDLQ error feedback is active even without calibration data
+(the rescaled Hessian is no longer the identity) and about a fifth of the
+int8 weights differ from the path above, so requesting them raises
+``NotImplementedError`` instead of silently computing something else: pass
+``actorder=False, use_diagonal_rescaling=False, use_random_permutation=False``.
+
+Also outside this path (``NotImplementedError``): a calibrated Hessian,
 learned rounding, greedy coordinate descent, SmoothQuant activation scales
 and the non-Hadamard orthogonal rotation.  Streaming / memory options are
 accepted and ignored (the whole weight lives in HBM).
@@ -31,17 +38,20 @@ from .. import _lib as L
 from .. import ops
 from ..utils.hadamard import next_power_of_two
 
+#: the keyword arguments that select the Hadamard/RTN path this converter implements
+HADAMARD_RTN = dict(actorder=False, use_diagonal_rescaling=False, use_random_permutation=False)
+
 
 class QuIPInt8Converter:
-    def __init__(self, block_size: int = 128, percdamp: float = 0.01, device: str = "cuda", actorder: bool = False,
+    def __init__(self, block_size: int = 128, percdamp: float = 0.01, device: str = "cuda", actorder: bool = True,
                  use_hadamard: bool = True, seed: Optional[int] = None, use_triton: bool = False,
                  lazy_updates: bool = True, use_learned_rounding: bool = False, ldlq_iterations: int = 1,
                  store_transformed: bool = False, streaming_mode: str = "balanced", streaming_thresholds=None,
                  no_memory_limits: bool = False, use_checkpointed_ldlq: bool = False,
                  checkpointed_ldlq_threshold: int = 8192, checkpoint_segments: int = 4,
                  requant_scheme: str = "tensor", requant_tensor_use_per_row_scale: bool = True,
-                 use_diagonal_rescaling: bool = False, use_frobenius_scaling: bool = True,
-                 use_random_permutation: bool = False, use_greedy_coordinate_descent: bool = False,
+                 use_diagonal_rescaling: bool = True, use_frobenius_scaling: bool = True,
+                 use_random_permutation: bool = True, use_greedy_coordinate_descent: bool = False,
                  greedy_cd_iterations: int = 100, frobenius_rho: float = 1.0):
         unsupported = {"actorder": actorder, "use_diagonal_rescaling": use_diagonal_rescaling,
                        "use_random_permutation": use_random_permutation,
@@ -50,7 +60,10 @@ class QuIPInt8Converter:
                        "use_hadamard=False": not use_hadamard}
         bad = [k for k, v in unsupported.items() if v]
         if bad:
-            raise NotImplementedError(f"QuIP options outside the Hadamard/RTN path: {', '.join(bad)}")
+            raise NotImplementedError(
+                f"QuIP options outside the Hadamard/RTN path: {', '.join(bad)} (the reference enables act-order, "
+                "diagonal rescaling and random permutation by default; pass actorder=False, "
+                "use_diagonal_rescaling=False, use_random_permutation=False for the implemented path)")
         if requant_scheme not in ("tensor", "block"):
             raise ValueError(f"requant_scheme must be 'tensor' or 'block', got {requant_scheme!r}")
         self.block_size = block_size

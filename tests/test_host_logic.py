@@ -7,7 +7,7 @@ import torch
 
 from convert_to_quant_quip_int8_b200 import _lib as L
 from convert_to_quant_quip_int8_b200 import ops
-from convert_to_quant_quip_int8_b200.converters.quip_int8 import QuIPInt8Converter
+from convert_to_quant_quip_int8_b200.converters.quip_int8 import HADAMARD_RTN, QuIPInt8Converter
 from convert_to_quant_quip_int8_b200.utils import comfy_quant as CQ
 from convert_to_quant_quip_int8_b200.utils.hadamard import hadamard_matrix, next_power_of_two
 from convert_to_quant_quip_int8_b200 import workloads as W
@@ -48,9 +48,9 @@ def test_quip_layer_tensor_names_and_dtypes():
 
 def test_converter_signs_match_reference(golden):
     g = golden("quip_convert.npz")
-    s_u, s_v = QuIPInt8Converter(seed=7).signs(128, 256)
+    s_u, s_v = QuIPInt8Converter(seed=7, **HADAMARD_RTN).signs(128, 256)
     assert np.array_equal(s_u.numpy(), g["s_u"]) and np.array_equal(s_v.numpy(), g["s_v"])
-    su2, sv2 = QuIPInt8Converter(seed=7).signs(96, 192)
+    su2, sv2 = QuIPInt8Converter(seed=7, **HADAMARD_RTN).signs(96, 192)
     assert np.array_equal(su2.numpy(), g["np_s_u"]) and np.array_equal(sv2.numpy(), g["np_s_v"])
 
 
@@ -95,6 +95,18 @@ def test_workload_definitions():
 
 def test_converter_rejects_options_on_cpu():
     with pytest.raises(NotImplementedError):
-        QuIPInt8Converter(use_random_permutation=True)
+        QuIPInt8Converter(use_random_permutation=True, actorder=False, use_diagonal_rescaling=False)
     with pytest.raises(ValueError):
-        QuIPInt8Converter(requant_scheme="axis")
+        QuIPInt8Converter(requant_scheme="axis", **HADAMARD_RTN)
+
+
+def test_converter_keeps_reference_defaults_and_refuses_them():
+    """The reference turns act-order, diagonal rescaling and random
+    permutation on by default (converters/quip_int8.py:33, 50, 52); a drop-in
+    call with default arguments must not silently run another algorithm."""
+    import inspect
+    sig = inspect.signature(QuIPInt8Converter.__init__).parameters
+    assert all(sig[k].default is True for k in HADAMARD_RTN)
+    with pytest.raises(NotImplementedError, match="actorder"):
+        QuIPInt8Converter()
+    QuIPInt8Converter(**HADAMARD_RTN)
