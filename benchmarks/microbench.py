@@ -3,6 +3,7 @@
     python benchmarks/microbench.py rotate   # K1 rotate+quant, K3 unrotate
     python benchmarks/microbench.py quant    # K1 per-token quant (+ fused GELU)
     python benchmarks/microbench.py gemm     # K2 block-scaled / per-row GEMM
+    python benchmarks/microbench.py gemm_stack  # K2 on the Flux / T5 stacks' largest linears
     python benchmarks/microbench.py convert  # K4 QuIP conversion
 
 Each case is timed with CUDA events around one launch, median of ``--iters``
@@ -108,6 +109,23 @@ def gemm_cases(run, dev):
     return res
 
 
+def gemm_stack_cases(run, dev):
+    """The stacks' largest GEMMs with per-row weight scales, bias and bf16
+    output: Flux single-block linear1 (4608 x 3072 -> 21504) first, then the
+    T5-XXL wi projection (4096 x 4096 -> 10240)."""
+    res = {}
+    for name, M, N, K in [("flux_linear1", 4608, 21504, 3072), ("t5_wi", 4096, 10240, 4096)]:
+        a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=dev)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+        sa = torch.rand(M, 1, device=dev) * 0.01
+        sb = torch.rand(N, device=dev) * 0.01
+        bias = torch.randn(N, device=dev).to(torch.bfloat16)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, sb, L.QI8_S_ROW, bias, torch.bfloat16, out=out))
+        res[f"k2_row_{name}_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+    return res
+
+
 def convert_cases(run, dev):
     res = {}
     for M, N in [(3072, 3072), (12288, 3072), (3072, 12288)]:
@@ -120,7 +138,8 @@ def convert_cases(run, dev):
     return res
 
 
-CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "convert": convert_cases}
+CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "gemm_stack": gemm_stack_cases,
+         "convert": convert_cases}
 
 
 def main(argv=None):
