@@ -55,8 +55,16 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     os.makedirs(BUILD_DIR, exist_ok=True)
     objs = []
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")]
+    headers.append(os.path.join(os.path.dirname(PKG), "include", "qi8.h"))
+    newest_header = max(os.path.getmtime(h) for h in headers if os.path.exists(h))
     for src in srcs:
         obj = os.path.join(BUILD_DIR, os.path.basename(src) + ".o")
+        # an object newer than its source and every shared header is current
+        if (not force and not ptxas_verbose and os.path.exists(obj)
+                and os.path.getmtime(obj) > max(os.path.getmtime(src), newest_header)):
+            objs.append(obj)
+            continue
         cmd = [nvcc, *NVCC_FLAGS, *extra, "-I", os.path.join(os.path.dirname(PKG), "include"),
                "-c", src, "-o", obj]
         if verbose:

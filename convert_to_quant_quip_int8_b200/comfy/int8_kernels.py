@@ -7,9 +7,9 @@ return dtypes; the arithmetic runs in libqi8 (see include/qi8.h):
                                            (comfy/int8_kernels.py:72-253)
 * ``act_dequant`` / ``weight_dequant``   (:126-179, :256-330)
 * ``int8_gemm`` / ``int8_addmm``         block-K promoted GEMM (:335-647)
-* ``int8_gemm_quant`` / ``int8_addmm_quant`` / ``int8_gelu``
-                                           output re-quantization chains
-                                           (:684-1312), composed from the above
+* ``int8_gemm_quant`` / ``int8_addmm_quant``  GEMM with the output
+                                           requantized in the epilogue (:684-1089)
+* ``int8_gelu``                          fused int8 GELU (:1122-1312)
 * ``quip_int8_matmul``                   transformed-space QuIP linear
                                            (:1374-1452), as W8A8: K1 rotate +
                                            per-token quant, tcgen05 GEMM, K3
@@ -90,22 +90,44 @@ def int8_addmm(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.T
     return _block_gemm(a, a_s, b, b_s, bias, input_block_size, out_dtype)
 
 
-def int8_gemm_quant(a, a_s, b, b_s, out_block_size: int = 128):
-    """GEMM followed by per-128-block output re-quantization (comfy/int8_kernels.py:920-996)."""
-    c = _block_gemm(a, a_s, b, b_s, None, 128, torch.float32)
-    return act_quant(c, out_block_size)
+def _quant_gemm(a, a_s, b, b_s, bias, out_block_size, input_block_size):
+    assert a.is_contiguous() and b.is_contiguous(), "Input tensors must be contiguous"
+    assert a_s.is_contiguous() and b_s.is_contiguous(), "Scaling tensors must be contiguous"
+    assert b.dim() == 2, f"Expected b to be 2D, got shape {b.shape}"
+    K = a.size(-1)
+    N = b.shape[0]
+    assert b.size(1) == K, f"Shape mismatch: b.shape={b.shape}, expected [..., {K}]"
+    assert N % out_block_size == 0, f"N={N} must be divisible by out_block_size={out_block_size}"
+    if out_block_size != 128 or input_block_size != 128:
+        raise NotImplementedError("the fused requantizing GEMM uses 128-element blocks")
+    return ops.gemm_i8_quant(a, b, a_s, b_s, bias, out_block_size)
 
 
-def int8_addmm_quant(a, a_s, b, b_s, bias=None, out_block_size: int = 128):
-    """GEMM + bias followed by per-128-block output re-quantization (:998-1089)."""
-    c = _block_gemm(a, a_s, b, b_s, bias, 128, torch.float32)
-    return act_quant(c, out_block_size)
+def int8_gemm_quant(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Tensor,
+                    out_block_size: int = 128, input_block_size: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``C_int8, C_scale = quantize(A @ B)`` in one kernel: the block-promoted
+    GEMM's epilogue requantizes every (row, 128-column block) of the fp32
+    result (comfy/int8_kernels.py:920-996)."""
+    return _quant_gemm(a, a_s, b, b_s, None, out_block_size, input_block_size)
 
 
-def int8_gelu(x: torch.Tensor, s_x: torch.Tensor, block_size: int = 128):
-    """Dequantize -> exact-erf GELU -> per-128-block re-quantization (:1234-1312)."""
-    y = act_dequant(x.contiguous(), s_x.contiguous(), block_size, torch.float32)
-    return act_quant(torch.nn.functional.gelu(y), block_size)
+def int8_addmm_quant(a: torch.Tensor, a_s: torch.Tensor, b: torch.Tensor, b_s: torch.Tensor,
+                     bias: Optional[torch.Tensor] = None, out_block_size: int = 128,
+                     input_block_size: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``C_int8, C_scale = quantize(A @ B + bias)`` in one kernel (:998-1089)."""
+    if bias is not None:
+        assert bias.is_contiguous(), "Bias tensor must be contiguous"
+    return _quant_gemm(a, a_s, b, b_s, bias, out_block_size, input_block_size)
+
+
+def int8_gelu(x: torch.Tensor, s_x: torch.Tensor, block_size: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``y_int8, y_scale = quantize(gelu(dequantize(x, s_x)))`` in one kernel (:1234-1312)."""
+    assert x.is_contiguous(), "Input tensor must be contiguous"
+    assert s_x.is_contiguous(), "Scale tensor must be contiguous"
+    assert x.size(-1) % block_size == 0, f"Last dimension must be divisible by block_size={block_size}"
+    if block_size != 128:
+        raise NotImplementedError("the fused int8 GELU uses 128-element blocks")
+    return ops.int8_gelu(x, s_x, block_size)
 
 
 def quip_int8_matmul(x: torch.Tensor, Q: torch.Tensor, scale: torch.Tensor, s_u: torch.Tensor,

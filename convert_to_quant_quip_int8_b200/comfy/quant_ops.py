@@ -395,17 +395,18 @@ LAYOUTS = {
 # ------------------------------------------------------------- handlers
 def _int8_gemm_or_fallback(a_int8, a_scale, b_int8, b_scale, block_size, bias=None, out_quant=False,
                            out_dtype=torch.bfloat16):
-    """Block-scaled GEMM (comfy/quant_ops.py:358-371) on the tcgen05 kernel."""
-    from .int8_kernels import act_quant
+    """Block-scaled GEMM (comfy/quant_ops.py:358-371) on the tcgen05 kernel;
+    with ``out_quant`` the epilogue requantizes the output per (row, block)
+    (the reference's int8_gemm_quant / int8_addmm_quant)."""
     K, batch, N = a_int8.shape[-1], a_int8.shape[:-1], b_int8.shape[0]
     a2 = a_int8.reshape(-1, K).contiguous()
     a_s2 = a_scale.reshape(-1, a_scale.shape[-1]).contiguous()
+    if out_quant:
+        q, s = ops.gemm_i8_quant(a2, b_int8.contiguous(), a_s2, b_scale.contiguous(), bias, block_size)
+        return q.reshape(*batch, N), s.reshape(*batch, N // block_size)
     b_kind = ops.scale_kind(b_scale, N, K, True, block_size)
     res = ops.gemm_i8(a2, b_int8.contiguous(), a_s2, L.QI8_S_ROW_KBLOCK, b_scale.contiguous(), b_kind, bias,
-                      torch.float32 if out_quant else out_dtype)
-    if out_quant:
-        q, s = act_quant(res, block_size)
-        return q.reshape(*batch, N), s.reshape(*batch, N // block_size)
+                      out_dtype)
     return res.reshape(*batch, N)
 
 

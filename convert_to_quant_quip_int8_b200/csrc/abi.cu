@@ -2,6 +2,7 @@
 // device status word written by kernels whose bounded waits expire.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -56,6 +57,14 @@ int fail(int code, const char* fmt, ...) {
 int check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return QI8_OK;
   return fail(QI8_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("QI8_PDL");
+    return v && *v && std::strcmp(v, "0") != 0;
+  }();
+  return on;
 }
 
 unsigned int* device_status_ptr() { return dev_info().status; }

@@ -96,6 +96,39 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// With QI8_PDL=1 the kernels of the inference path are launched with
+// programmatic stream serialization: a kernel may be scheduled while the
+// previous kernel on the stream is still finishing, runs its prologue
+// (barrier init, TMEM allocation, descriptor prefetch), and waits in
+// pdl_wait() -- before its first global-memory access -- until that kernel
+// has completed and its writes are visible.  Without the launch attribute
+// both are no-ops.  Off by default: on the Flux-shaped stack (one CUDA graph
+// of 456 launches) it measured 34.1 ms per forward against 32.9 ms without.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel on the stream be scheduled (it still waits in pdl_wait).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// True when QI8_PDL is set to a value other than 0 (read once per process).
+bool pdl_enabled();
+
+// Launches kern<<<grid, block, smem, st>>>(args...) with programmatic stream
+// serialization when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Exact-erf GELU on an fp32 value (torch F.gelu default formula).
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));

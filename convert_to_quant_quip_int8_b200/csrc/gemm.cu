@@ -108,6 +108,14 @@ struct GemmExt {
   // gather), which receive the same tile at the same offset.
   int n_outs;
   void* outs[QI8_MAX_PEERS];
+  // int8 output (out_dtype QI8_I8, non-swapped block-scaled kernels only):
+  // every (row, 128-column block) of the fp32 result is requantized with
+  // scale = max(amax / 127, 1e-8), q = trunc(clamp(y / scale, +-127)); the
+  // scales go to q_scale [M, N / 128].  The K-block promotion then follows
+  // the reference's order, acc + (fp32(p) * a_s) * b_s, in separately
+  // rounded operations.
+  float* q_scale;
+  int exact;
 };
 
 // Calls f(base) for every output destination (static indices, so the
@@ -614,6 +622,45 @@ __device__ __forceinline__ void finalize_tile(const GemmArgs& p, const GemmExt& 
   }
 }
 
+// Tile epilogue with int8 output (fused output requantization of the
+// reference's int8_gemm_quant / int8_addmm_quant, comfy/int8_kernels.py:
+// 684-917): thread = token rr, its 128 accumulator columns are the output
+// columns cc0 .. cc0 + 127, i.e. exactly one 128-column quantization block.
+// y = acc * frow * col_scale + bias (unit factors for block scales), then
+// scale = max(amax / 127, 1e-8) and q = trunc(clamp(y / scale, -127, 127)).
+__device__ __forceinline__ void finalize_tile_q8(const GemmArgs& p, const GemmExt& e, float2 (&acc)[64],
+                                                 const float* my_col, const float* my_bias, float frow, int rr,
+                                                 int cc0) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float y0 = __fadd_rn(__fmul_rn(__fmul_rn(acc[i].x, frow), my_col[2 * i]), my_bias[2 * i]);
+    const float y1 = __fadd_rn(__fmul_rn(__fmul_rn(acc[i].y, frow), my_col[2 * i + 1]), my_bias[2 * i + 1]);
+    acc[i] = make_float2(y0, y1);
+    amax = fmaxf(amax, fmaxf(fabsf(y0), fabsf(y1)));
+  }
+  const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+  uint4* q = reinterpret_cast<uint4*>(static_cast<int8_t*>(p.out) + (int64_t)rr * p.ld_out + cc0);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int b = 0; b < 4; b += 2) {
+        const float2 y = acc[g * 8 + k * 2 + (b >> 1)];
+        const int q0 = __float2int_rz(fminf(fmaxf(__fdiv_rn(y.x, scale), -127.0f), 127.0f));
+        const int q1 = __float2int_rz(fminf(fmaxf(__fdiv_rn(y.y, scale), -127.0f), 127.0f));
+        word |= ((uint32_t)(q0 & 0xFF) << (8 * b)) | ((uint32_t)(q1 & 0xFF) << (8 * (b + 1)));
+      }
+      w[k] = word;
+    }
+    q[g] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  e.q_scale[(int64_t)rr * (p.N >> 7) + (cc0 >> 7)] = scale;
+}
+
 // SWAP: the weight tile is the MMA A operand (TMEM lanes = output features)
 // and the activation tile the B operand (TMEM columns = tokens).  Used when
 // the weight scale varies per (row, K block) and the activation scale does
@@ -672,6 +719,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // everything above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const int KB = p.KB;
   if (warp >= NUM_EPI_WARPS) {
@@ -832,14 +883,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool a_kb = !SWAP && p.a_kind == QI8_S_ROW_KBLOCK;
         const bool b_col = !SWAP && p.b_kind == QI8_S_ROW_KBLOCK;
         const bool b_tile = p.b_kind == QI8_S_TILE128;
+        const bool exact = !SWAP && e.exact;
         for (int kb = 0; kb < KB; ++kb, ++au) {
           const int buf = au & 1;
-          float sk = 1.0f;
+          float sk = 1.0f, ska = 1.0f, skb = 1.0f;
           if constexpr (SWAP) {
             sk = row_ok ? __ldg(p.b_scale + (int64_t)rr * KB + kb) : 0.0f;
           } else {
-            if (a_kb) sk = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
-            if (b_tile) sk = __fmul_rn(sk, cols_ok ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f);
+            if (a_kb) sk = ska = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
+            if (b_tile) skb = cols_ok ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f;
+            if (b_tile) sk = __fmul_rn(sk, skb);
             if (b_col) {
               __syncwarp();
 #pragma unroll
@@ -872,15 +925,27 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty_bar(buf, half));
               }
+              if (exact) {
+                // the reference's order: acc + (fp32(p) * a_s) * b_s, each rounded
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int col = c * 32 + 2 * j;
-                // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
-                const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
-                                             __int2float_rn((int)rb[c & 1][2 * j + 1]));
-                float2 sc = sk2;
-                if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
-                acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  const float b0 = b_col ? my_kb[col] : skb, b1 = b_col ? my_kb[col + 1] : skb;
+                  const float f0 = __int2float_rn((int)rb[c & 1][2 * j]), f1 = __int2float_rn((int)rb[c & 1][2 * j + 1]);
+                  acc[col >> 1].x = __fadd_rn(acc[col >> 1].x, __fmul_rn(__fmul_rn(f0, ska), b0));
+                  acc[col >> 1].y = __fadd_rn(acc[col >> 1].y, __fmul_rn(__fmul_rn(f1, ska), b1));
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
+                  const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                               __int2float_rn((int)rb[c & 1][2 * j + 1]));
+                  float2 sc = sk2;
+                  if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
+                  acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                }
               }
             }
           }
@@ -890,6 +955,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         // already released, so the next tile's MMAs overlap these stores)
         // SWAP transposes through shared memory with __syncwarp, so the whole
         // warp enters together; lanes whose row is out of range store nothing
+        if constexpr (!SWAP && !MULTI) {
+          if (p.out_dtype == QI8_I8) {
+            if (cols_ok && row_ok) finalize_tile_q8(p, e, acc, my_col, my_bias, frow, rr, cc0);
+            continue;
+          }
+        }
         if (cols_ok && (SWAP || row_ok)) {
           if (p.act == QI8_ACT_GELU)
             finalize_tile<SWAP, true, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc0 + 64, R, C, warp, lane, sxp);
@@ -1089,6 +1160,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
+  // everything above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed
+  pdl_wait();
+  pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const int KB = p.KB;
   const int r_ptiles = p.r_tiles;  // tiles of 256 rows over the TMEM-lane operand
@@ -1230,6 +1305,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const bool a_kb = !SWAP && p.a_kind == QI8_S_ROW_KBLOCK;
         const bool b_col = !SWAP && p.b_kind == QI8_S_ROW_KBLOCK;
         const bool b_tile = p.b_kind == QI8_S_TILE128;
+        const bool exact = !SWAP && e.exact;
         // SWAP: this row's K-block weight scales, loaded two K blocks ahead
         const float* srow = p.b_scale + (int64_t)(row_ok ? rr : 0) * KB;
         float sk_n1 = 0.0f, sk_n2 = 0.0f;
@@ -1240,16 +1316,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < KB; ++kb, ++au) {
           const int buf = au & 1;
           // scale of the first and of the second 64-column run
-          float sk0 = 1.0f, sk1 = 1.0f;
+          float sk0 = 1.0f, sk1 = 1.0f, ska = 1.0f, skb0 = 1.0f, skb1 = 1.0f;
           if constexpr (SWAP) {
             sk0 = sk1 = sk_n1;
             sk_n1 = sk_n2;
             sk_n2 = (row_ok && kb + 2 < KB) ? __ldg(srow + kb + 2) : 0.0f;
           } else {
-            if (a_kb) sk0 = sk1 = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
+            if (a_kb) sk0 = sk1 = ska = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
             if (b_tile) {
-              sk0 = __fmul_rn(sk0, cc0 < C ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f);
-              sk1 = __fmul_rn(sk1, cc1 < C ? __ldg(p.b_scale + (int64_t)(cc1 >> 7) * KB + kb) : 0.0f);
+              skb0 = cc0 < C ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f;
+              skb1 = cc1 < C ? __ldg(p.b_scale + (int64_t)(cc1 >> 7) * KB + kb) : 0.0f;
+              sk0 = __fmul_rn(sk0, skb0);
+              sk1 = __fmul_rn(sk1, skb1);
             }
             if (b_col) {
               __syncwarp();
@@ -1283,20 +1361,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               }
               const float skc = c < 2 ? sk0 : sk1;
               const float2 sk2 = make_float2(skc, skc);
+              if (exact) {
+                // the reference's order: acc + (fp32(p) * a_s) * b_s, each rounded
+                const float skbc = c < 2 ? skb0 : skb1;
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int col = c * 32 + 2 * j;
-                // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
-                const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
-                                             __int2float_rn((int)rb[c & 1][2 * j + 1]));
-                float2 sc = sk2;
-                if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
-                acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  const float b0 = b_col ? my_kb[col] : skbc, b1 = b_col ? my_kb[col + 1] : skbc;
+                  const float f0 = __int2float_rn((int)rb[c & 1][2 * j]), f1 = __int2float_rn((int)rb[c & 1][2 * j + 1]);
+                  acc[col >> 1].x = __fadd_rn(acc[col >> 1].x, __fmul_rn(__fmul_rn(f0, ska), b0));
+                  acc[col >> 1].y = __fadd_rn(acc[col >> 1].y, __fmul_rn(__fmul_rn(f1, ska), b1));
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
+                  const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                               __int2float_rn((int)rb[c & 1][2 * j + 1]));
+                  float2 sc = sk2;
+                  if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
+                  acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                }
               }
             }
           }
         }
         if (!ok) break;
+        if constexpr (!SWAP && !MULTI && !SPLIT) {
+          if (p.out_dtype == QI8_I8) {
+            if (cols_ok && row_ok) finalize_tile_q8(p, e, acc, my_col, my_bias, frow, rr, cc0);
+            continue;
+          }
+        }
         if (cols_ok && (SWAP || row_ok)) {
           if (p.act == QI8_ACT_GELU)
             finalize_tile<SWAP, true, MULTI>(p, e, acc, my_col, my_bias, frow, brow, rr, cc0, cc1, R, C, warp, lane, sxp);
@@ -1464,8 +1561,8 @@ int launch_pair(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs
   const int maxc = pair_max_clusters<PROMOTE, SWAP, MULTI, SPLIT>(dev);
   if (maxc <= 0) return QI8_EUNSUPPORTED;
   const int ncl = p.num_tiles < maxc ? p.num_tiles : maxc;
-  kern<<<2 * ncl, THREADS, pairk::P_SMEM, st>>>(mapA, mapB, p, e);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = launch_pdl(kern, dim3(2 * ncl), dim3(THREADS), pairk::P_SMEM, st, mapA, mapB, p, e);
+  if (err == cudaSuccess) err = cudaGetLastError();
   if (err != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, kern);
@@ -1483,6 +1580,8 @@ __global__ void splitk_finalize_kernel(const int32_t* __restrict__ ws, int S, in
                                        const float* __restrict__ a_scale, int a_kind, const float* __restrict__ b_scale,
                                        int b_kind, const void* __restrict__ bias, int bias_dtype, void* out,
                                        int out_dtype, int64_t ld_out, int act) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int nq = N >> 2;
   const int64_t total = (int64_t)M * nq;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1552,7 +1651,7 @@ namespace {
 int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K, const float* a_scale, int a_kind,
                 const float* b_scale, int b_kind, const void* bias, int bias_dtype, void* const* outs, int n_outs,
                 int out_dtype, int64_t ld_out, int act, void* stream, void* workspace = nullptr,
-                int64_t workspace_bytes = 0) {
+                int64_t workspace_bytes = 0, float* q_scale = nullptr) {
   QI8_REQUIRE(device_ok(), QI8_EUNSUPPORTED, "no sm_100 device current");
   QI8_REQUIRE(A && B && outs && n_outs >= 1 && n_outs <= QI8_MAX_PEERS, QI8_EINVAL, "null pointer or bad n_outs");
   for (int d = 0; d < n_outs; ++d) QI8_REQUIRE(outs[d], QI8_EINVAL, "null output pointer %d", d);
@@ -1567,7 +1666,8 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   QI8_REQUIRE(b_kind >= QI8_S_NONE && b_kind <= QI8_S_TILE128, QI8_EINVAL, "b_kind %d", b_kind);
   QI8_REQUIRE((a_kind == QI8_S_NONE) == (a_scale == nullptr), QI8_EINVAL, "a_scale/a_kind mismatch");
   QI8_REQUIRE((b_kind == QI8_S_NONE) == (b_scale == nullptr), QI8_EINVAL, "b_scale/b_kind mismatch");
-  QI8_REQUIRE(out_dtype == QI8_BF16 || out_dtype == QI8_F16 || out_dtype == QI8_F32 || out_dtype == QI8_I32,
+  QI8_REQUIRE(out_dtype == QI8_BF16 || out_dtype == QI8_F16 || out_dtype == QI8_F32 || out_dtype == QI8_I32 ||
+                  (out_dtype == QI8_I8 && q_scale),
               QI8_EDTYPE, "out dtype %d", out_dtype);
   QI8_REQUIRE(!bias || bias_dtype == QI8_BF16 || bias_dtype == QI8_F16 || bias_dtype == QI8_F32, QI8_EDTYPE,
               "bias dtype %d", bias_dtype);
@@ -1580,6 +1680,14 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     QI8_REQUIRE(!promote && a_kind == QI8_S_NONE && b_kind == QI8_S_NONE && !bias && act == QI8_ACT_NONE,
                 QI8_EINVAL, "int32 output takes no scales, bias or activation");
   QI8_REQUIRE(act == QI8_ACT_NONE || act == QI8_ACT_GELU, QI8_EINVAL, "act %d", act);
+  if (out_dtype == QI8_I8) {
+    // fused output requantization: block-scaled activations and weights, one destination
+    QI8_REQUIRE(a_kind == QI8_S_ROW_KBLOCK && (b_kind == QI8_S_TILE128 || b_kind == QI8_S_ROW_KBLOCK), QI8_EINVAL,
+                "int8 output needs per-(row, K block) activation scales and 128-block weight scales");
+    QI8_REQUIRE(n_outs == 1 && act == QI8_ACT_NONE, QI8_EINVAL, "int8 output has one destination and no activation");
+    QI8_REQUIRE(N % 128 == 0, QI8_ESHAPE, "N=%lld must be divisible by out_block_size=128", (long long)N);
+    QI8_REQUIRE((reinterpret_cast<uintptr_t>(q_scale) & 3) == 0, QI8_EALIGN, "scale_out must be 4-byte aligned");
+  }
   if (M == 0) return QI8_OK;
 
   // weights on TMEM lanes when their scale varies per (row, K block) and the activations' does not
@@ -1590,7 +1698,16 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   int dev = 0;
   QI8_CUDA(cudaGetDevice(&dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (Rrows > BM) {
+  // a plain GEMM whose output tiles fill few CTA pairs splits K when the
+  // caller gives a workspace, also with at most 128 rows (the pair tile's
+  // rows beyond M are zero-filled by TMA and never stored)
+  bool split_small = false;
+  if (Rrows <= BM && !promote && n_outs == 1 && workspace && out_dtype != QI8_I8) {
+    int kb_split = 0;
+    const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
+    split_small = S > 1 && workspace_bytes >= (int64_t)S * M * N * 4;
+  }
+  if (Rrows > BM || split_small) {
     // CTA pairs: 256 rows on TMEM lanes x 256 columns per pair tile
     GemmArgs p{};
     const int bnp = pairk::PBN;
@@ -1602,6 +1719,8 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
     GemmExt e{};
     set_outs(p, e, outs, n_outs);
+    e.q_scale = q_scale;
+    e.exact = out_dtype == QI8_I8;
     p.act = act;
     p.status = device_status_ptr();
     e.kb_split = p.KB;
@@ -1631,10 +1750,10 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
         int64_t blocks = (work + 255) / 256;
         const int64_t cap = (int64_t)(sm_count() > 0 ? sm_count() : 148) * 8;
         if (blocks > cap) blocks = cap;
-        splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const int32_t*>(workspace), S, M * N,
-                                                                 (int)M, (int)N, a_scale, a_kind, b_scale, b_kind,
-                                                                 bias, bias_dtype, outs[0], out_dtype, ld_out, act);
-        return check_cuda(cudaGetLastError(), "splitk_finalize_kernel launch");
+        return check_cuda(launch_pdl(splitk_finalize_kernel, dim3((unsigned)blocks), dim3(256), 0, st,
+                                     static_cast<const int32_t*>(workspace), S, M * N, (int)M, (int)N, a_scale, a_kind,
+                                     b_scale, b_kind, bias, bias_dtype, outs[0], out_dtype, ld_out, act),
+                          "splitk_finalize_kernel launch");
       }
     }
     if (n_outs > 1) {
@@ -1661,6 +1780,8 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   p.bias = bias; p.bias_dtype = bias_dtype; p.out_dtype = out_dtype; p.ld_out = ld_out;
   GemmExt e{};
   set_outs(p, e, outs, n_outs);
+  e.q_scale = q_scale;
+  e.exact = out_dtype == QI8_I8;
   e.kb_split = p.KB;
   p.act = act;
   p.status = device_status_ptr();
@@ -1685,8 +1806,9 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   }
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-  kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(mapA, mapB, p, e);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, static_cast<cudaStream_t>(stream), mapA,
+                               mapB, p, e);
+  if (err == cudaSuccess) err = cudaGetLastError();
   if (err != cudaSuccess) {
     cudaFuncAttributes fa{};
     cudaFuncGetAttributes(&fa, kern);
@@ -1707,8 +1829,19 @@ extern "C" int qi8_gemm_i8(const int8_t* A, const int8_t* B, int64_t M, int64_t 
                      act, stream);
 }
 
+extern "C" int qi8_gemm_i8_quant(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K,
+                                 const float* a_scale, int a_kind, const float* b_scale, int b_kind, const void* bias,
+                                 int bias_dtype, int8_t* q_out, int64_t ld_q, float* scale_out, int out_block,
+                                 void* stream) {
+  QI8_REQUIRE(out_block == 128, QI8_ESHAPE, "out_block_size %d: the fused requantization uses 128", out_block);
+  QI8_REQUIRE(scale_out, QI8_EINVAL, "null scale_out");
+  void* outs[1] = {q_out};
+  return gemm_launch(A, B, M, N, K, a_scale, a_kind, b_scale, b_kind, bias, bias_dtype, outs, 1, QI8_I8, ld_q,
+                     QI8_ACT_NONE, stream, nullptr, 0, scale_out);
+}
+
 extern "C" int64_t qi8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int a_kind, int b_kind) {
-  if (!device_ok() || M <= 128 || N <= 0 || K <= 0) return 0;
+  if (!device_ok() || M <= 0 || N <= 0 || K <= 0) return 0;
   if (a_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_ROW_KBLOCK || b_kind == QI8_S_TILE128) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;

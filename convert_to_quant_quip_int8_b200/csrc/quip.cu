@@ -47,28 +47,63 @@ struct ColArgs {
 
 enum { FINAL_NONE = 0, FINAL_MUL = 1, FINAL_DIV = 2 };
 
+// One round of the column transform: the RB butterfly stages of strides
+// 2^s .. 2^(s+RB-1) (in rows of the strip) on groups of 2^RB rows held in
+// registers, one column per lane.  Stages run in ascending stride order, as
+// in the reference's FWHT, so every element sees the same operations.
+template <int RB>
+__device__ __forceinline__ void col_round(float* tile, int R, int s, int warp, int nw, int lane) {
+  constexpr int G = 1 << RB;
+  const int groups = R >> RB;
+  const int lo_mask = (1 << s) - 1;
+  for (int g = warp; g < groups; g += nw) {
+    const int base = (g & lo_mask) | ((g >> s) << (s + RB));
+    float v[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) v[j] = tile[(base | (j << s)) * COL_STRIP + lane];
+#pragma unroll
+    for (int b = 0; b < RB; ++b) {
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        if (j & (1 << b)) continue;
+        const float x = v[j], y = v[j | (1 << b)];
+        v[j] = x + y;
+        v[j | (1 << b)] = x - y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) tile[(base | (j << s)) * COL_STRIP + lane] = v[j];
+  }
+}
+
+// Column (M-direction) FWHT over row-index bits [b0, b0 + rbits) of X: a CTA
+// holds a strip of R = 2^rbits rows (stride 2^b0 apart) x 32 columns in shared
+// memory (bank = lane, conflict-free), runs the stages in rounds of up to
+// four bits in registers, and writes the strip back.  Loads and stores are
+// 128-byte row segments per warp.
 template <bool LOAD_W, int FINAL, bool SIGN_OUT>
 __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
   extern __shared__ float tile[];  // [R][COL_STRIP]
   const int R = 1 << a.rbits;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int NW = COL_THREADS / 32;
+  const int nw = blockDim.x >> 5;
   const int64_t j = (int64_t)blockIdx.x * COL_STRIP + lane;
   const bool col_ok = j < a.N_pad;
   const int64_t lo_count = int64_t(1) << a.b0;
   const int64_t lo = blockIdx.y % lo_count, hi = blockIdx.y / lo_count;
   const int64_t hi_base = lo + (hi << (a.b0 + a.rbits));
 
-  // unrolled so that a warp keeps several row loads in flight
-#pragma unroll 8
-  for (int k = warp; k < R; k += NW) {
+  float sv = 1.0f;
+  if constexpr (LOAD_W) sv = (col_ok && j < a.N_pad) ? __ldg(a.s_v + j) : 0.0f;
+#pragma unroll 16
+  for (int k = warp; k < R; k += nw) {
     const int64_t i = hi_base + ((int64_t)k << a.b0);
     float v = 0.0f;
     if (col_ok) {
       if constexpr (LOAD_W) {
         v = (i < a.M && j < a.N) ? load_as_f32(a.w, a.w_dtype, i * a.N + j) : 0.0f;
         v = __fmul_rn(v, __ldg(a.s_u + i));
-        v = __fmul_rn(v, __ldg(a.s_v + j));
+        v = __fmul_rn(v, sv);
       } else {
         v = a.x[i * a.ld_x + j];
       }
@@ -76,19 +111,17 @@ __global__ void __launch_bounds__(COL_THREADS) col_fwht_kernel(ColArgs a) {
     tile[k * COL_STRIP + lane] = v;
   }
   __syncthreads();
-  for (int h = 1; h < R; h <<= 1) {
-#pragma unroll 4
-    for (int p = warp; p < (R >> 1); p += NW) {
-      const int k = ((p / h) * 2 * h) + (p % h);
-      const float lo_v = tile[k * COL_STRIP + lane];
-      const float hi_v = tile[(k + h) * COL_STRIP + lane];
-      tile[k * COL_STRIP + lane] = lo_v + hi_v;
-      tile[(k + h) * COL_STRIP + lane] = lo_v - hi_v;
+  for (int s = 0; s < a.rbits; s += 4) {
+    switch (a.rbits - s >= 4 ? 4 : a.rbits - s) {
+      case 4: col_round<4>(tile, R, s, warp, nw, lane); break;
+      case 3: col_round<3>(tile, R, s, warp, nw, lane); break;
+      case 2: col_round<2>(tile, R, s, warp, nw, lane); break;
+      default: col_round<1>(tile, R, s, warp, nw, lane); break;
     }
     __syncthreads();
   }
-#pragma unroll 8
-  for (int k = warp; k < R; k += NW) {
+#pragma unroll 16
+  for (int k = warp; k < R; k += nw) {
     const int64_t i = hi_base + ((int64_t)k << a.b0);
     float v = tile[k * COL_STRIP + lane];
     if constexpr (FINAL == FINAL_MUL) v = __fmul_rn(v, a.norm);
@@ -272,9 +305,11 @@ int64_t next_pow2(int64_t n) {
 // selects the normalization of the last pass.
 int col_passes(bool forward, const ColArgs& base, cudaStream_t st, int final = FINAL_MUL) {
   const int L = log2_exact(base.M_pad);
+  // one pass up to COL_MAX_BITS bits, otherwise two balanced passes
+  const int first_bits = L <= COL_MAX_BITS ? L : (L + 1) / 2;
   int b0 = 0;
   while (b0 < L || (L == 0 && b0 == 0)) {
-    const int rb = (L - b0) > COL_MAX_BITS ? COL_MAX_BITS : (L - b0);
+    const int rb = b0 == 0 ? first_bits : (L - b0);
     ColArgs a = base;
     a.b0 = b0;
     a.rbits = rb;
@@ -295,7 +330,9 @@ int col_passes(bool forward, const ColArgs& base, cudaStream_t st, int final = F
       kern = col_fwht_kernel<false, FINAL_MUL, true>;
     }
     if (smem > 48 * 1024) QI8_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<grid, COL_THREADS, smem, st>>>(a);
+    // enough warps for the radix-16 rounds of a strip: R / 16 groups, at most COL_THREADS / 32 warps
+    const int warps = rb >= 7 ? COL_THREADS / 32 : (rb >= 4 ? (1 << (rb - 4)) : 1);
+    kern<<<grid, warps * 32, smem, st>>>(a);
     QI8_CUDA(cudaGetLastError());
     if (L == 0) break;
     b0 += rb;

@@ -733,6 +733,8 @@ __global__ void __launch_bounds__(256, 3) token_rows_kernel(QArgs a, int rows, i
     __syncthreads();
   }
   const uint16_t* gtab = reinterpret_cast<const uint16_t*>(gtab_w);
+  pdl_wait();
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rpb = 8 / W, wr = warp % W, rsub = warp / W;
   const int nc = a.n / EPC;
@@ -833,8 +835,8 @@ int launch_cpl(const QArgs& a, int rows, int W, cudaStream_t st) {
   const int64_t groups = (rows + rpb - 1) / rpb;
   const int64_t cap = (int64_t)sm_count() * per_sm;
   const unsigned grid = (unsigned)(groups < cap ? groups : (cap > 0 ? cap : 1));
-  token_rows_kernel<T, CPL, GELU><<<grid, 256, 0, st>>>(a, rows, W);
-  return check_cuda(cudaGetLastError(), "token_rows_kernel launch");
+  return check_cuda(launch_pdl(token_rows_kernel<T, CPL, GELU>, dim3(grid), dim3(256), 0, st, a, rows, W),
+                    "token_rows_kernel launch");
 }
 
 // Returns -1 when the row shape is outside this path (caller falls back).

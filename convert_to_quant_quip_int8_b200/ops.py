@@ -174,6 +174,46 @@ def gemm_i8(a: torch.Tensor, b: torch.Tensor, a_scale: Optional[torch.Tensor] = 
     return out.reshape(*a.shape[:-1], N)
 
 
+def gemm_i8_quant(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor,
+                  bias: Optional[torch.Tensor] = None, out_block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """K2 with the output requantized per (row, 128-column block) in the
+    epilogue: ``a [..., K]`` int8 with block scales ``[..., K/128]``, ``b [N, K]``
+    with ``[N/128, K/128]`` tile or ``[N, K/128]`` row-block scales.  Returns
+    ``(q int8 [..., N], scale fp32 [..., N/128])``."""
+    L.require_cuda(a, b)
+    assert a.dtype == torch.int8 and b.dtype == torch.int8, "int8 operands required"
+    a2 = a.reshape(-1, a.shape[-1])
+    assert a2.is_contiguous() and b.is_contiguous() and b.dim() == 2, "Input tensors must be contiguous"
+    M, K = a2.shape
+    N = b.shape[0]
+    assert b.shape[1] == K, f"Shape mismatch: b.shape={tuple(b.shape)}, expected [N, {K}]"
+    assert N % out_block == 0, f"N={N} must be divisible by out_block_size={out_block}"
+    a_scale = a_scale.to(torch.float32).contiguous()
+    b_scale = b_scale.to(torch.float32).contiguous()
+    assert a_scale.numel() == M * (K // 128), f"activation scales of shape {tuple(a_scale.shape)}"
+    b_kind = L.QI8_S_ROW_KBLOCK if b_scale.numel() == N * (K // 128) else scale_kind(b_scale, N, K, True)
+    q = torch.empty((M, N), dtype=torch.int8, device=a.device)
+    s = torch.empty((M, N // out_block), dtype=torch.float32, device=a.device)
+    bb = None if bias is None else bias.contiguous()
+    L.check(L.load().qi8_gemm_i8_quant(L.ptr(a2), L.ptr(b), M, N, K, L.ptr(a_scale), L.QI8_S_ROW_KBLOCK,
+                                       L.ptr(b_scale), b_kind, L.ptr(bb), L.dtype_code(bb.dtype) if bb is not None else 0,
+                                       L.ptr(q), N, L.ptr(s), out_block, L.stream_ptr(a.device)), "qi8_gemm_i8_quant")
+    return q.reshape(*a.shape[:-1], N), s.reshape(*a.shape[:-1], N // out_block)
+
+
+def int8_gelu(q: torch.Tensor, scale: torch.Tensor, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """GELU of a block-quantized int8 activation, requantized per block."""
+    L.require_cuda(q, scale)
+    assert q.dtype == torch.int8 and q.is_contiguous() and scale.is_contiguous(), "Input tensors must be contiguous"
+    n = q.shape[-1]
+    rows = q.numel() // n
+    q_out = torch.empty_like(q)
+    s_out = torch.empty(scale.shape, dtype=torch.float32, device=q.device)
+    L.check(L.load().qi8_int8_gelu(L.ptr(q), L.ptr(scale.to(torch.float32)), rows, n, block, L.ptr(q_out),
+                                   L.ptr(s_out), L.stream_ptr(q.device)), "qi8_int8_gelu")
+    return q_out, s_out
+
+
 _WS_CACHE = {}
 
 

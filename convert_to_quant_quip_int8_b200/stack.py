@@ -165,6 +165,14 @@ class LinearStack:
         max_tn = max(s.tokens * s.n for s in self.specs)
         self.xq = torch.empty(max_tk, dtype=torch.int8, device=dev)
         self.xs = torch.empty(max_t, dtype=torch.float32, device=dev)
+        # split-K workspace: GEMMs whose output tiles fill few CTA pairs (the
+        # small token counts of a token split, or a thin output) split K into
+        # exact int32 partial planes reduced by a second pass
+        self.ws_bytes = 0
+        if not self.sharded:
+            self.ws_bytes = max(int(self.lib.qi8_gemm_workspace_bytes(s.tokens, s.n, s.k, L.QI8_S_ROW, L.QI8_S_ROW))
+                                for s in self.specs)
+        self.ws = torch.empty(max(self.ws_bytes, 16), dtype=torch.uint8, device=dev)
         # consumed outputs get their own buffer per (tokens, n); the rest share a scratch
         keys = []
         for s in self.specs:
@@ -204,9 +212,10 @@ class LinearStack:
         n = q.shape[0]
         a = self.xq.data_ptr() + lo * s.k
         xs = self.xs.data_ptr() + lo * 4
-        L.check(self.lib.qi8_gemm_i8(ctypes.c_void_p(a), L.ptr(q), hi - lo, n, s.k, ctypes.c_void_p(xs), L.QI8_S_ROW,
-                                     L.ptr(sc), L.QI8_S_ROW, L.ptr(bias), L.QI8_BF16 if bias is not None else 0,
-                                     ctypes.c_void_p(out_ptr), L.QI8_BF16, ld_out, L.QI8_ACT_NONE, sp), "qi8_gemm_i8")
+        L.check(self.lib.qi8_gemm_i8_ws(ctypes.c_void_p(a), L.ptr(q), hi - lo, n, s.k, ctypes.c_void_p(xs),
+                                        L.QI8_S_ROW, L.ptr(sc), L.QI8_S_ROW, L.ptr(bias),
+                                        L.QI8_BF16 if bias is not None else 0, ctypes.c_void_p(out_ptr), L.QI8_BF16,
+                                        ld_out, L.QI8_ACT_NONE, L.ptr(self.ws), self.ws_bytes, sp), "qi8_gemm_i8_ws")
 
     def run_linear(self, i: int, sp, events=None):
         s = self.specs[i]
@@ -255,7 +264,10 @@ class LinearStack:
     def launches_per_forward(self) -> int:
         """Kernels of this library launched by one forward (K1 + GEMMs + layouts)."""
         if not self.sharded:
-            return 2 * len(self.specs)
+            # K1 + GEMM, plus the reduce pass of every GEMM that splits K
+            split = sum(1 for s in self.specs
+                        if self.lib.qi8_gemm_workspace_bytes(s.tokens, s.n, s.k, L.QI8_S_ROW, L.QI8_S_ROW) > 0)
+            return 2 * len(self.specs) + split
         if self.peer is not None:
             return 3 * len(self.specs)  # K1, fused GEMM + gather, peer barrier
         return sum(1 + 2 * len(token_chunks(s.tokens, self.chunks)) for s in self.specs)

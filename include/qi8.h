@@ -262,6 +262,31 @@ QI8_API int qi8_gemm_i8_ws(const int8_t* A, const int8_t* B, int64_t M, int64_t 
                            int out_dtype, int64_t ld_out, int act, void* workspace, int64_t workspace_bytes,
                            void* stream);
 
+/* K2 with the output requantized in the epilogue (replaces int8_gemm_quant /
+   int8_addmm_quant, comfy/int8_kernels.py:684-1089, used by the
+   BlockWiseINT8Layout linear with out_quant=True, comfy/quant_ops.py:362-364).
+   A [M, K] int8 with a_scale [M, K/128] (a_kind QI8_S_ROW_KBLOCK), B [N, K]
+   int8 with b_scale [N/128, K/128] (QI8_S_TILE128) or [N, K/128]
+   (QI8_S_ROW_KBLOCK); bias (or null) [N].  acc accumulates
+   fp32(A_kb B_kb^T) * a_s * b_s in K-block order (separately rounded, as the
+   reference), + bias; then per (row, 128-column block):
+   scale = max(amax / 127, 1e-8), q = trunc(clamp(acc / scale, -127, 127)).
+   q_out [M, ld_q] int8 (ld_q % 16 == 0), scale_out [M, N/128] fp32;
+   N % 128 == 0, out_block must be 128. */
+QI8_API int qi8_gemm_i8_quant(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t K,
+                              const float* a_scale, int a_kind, const float* b_scale, int b_kind, const void* bias,
+                              int bias_dtype, int8_t* q_out, int64_t ld_q, float* scale_out, int out_block,
+                              void* stream);
+
+/* Fused int8 GELU (replaces int8_gelu, comfy/int8_kernels.py:1122-1312, the
+   BlockWiseINT8Layout aten.gelu handler, comfy/quant_ops.py:435-448):
+   v = q * scale per (row, 128-block), g = (v * 0.5) * (1 + erf(v / 1.41421356237))
+   with erf correctly rounded to fp32, then the same per-block requantization
+   as qi8_gemm_i8_quant.  q, q_out [rows, n] int8 (4-byte aligned), scale and
+   scale_out [rows, n/128]; n % 128 == 0, block must be 128. */
+QI8_API int qi8_int8_gelu(const int8_t* q, const float* scale, int64_t rows, int64_t n, int block, int8_t* q_out,
+                          float* scale_out, void* stream);
+
 /* Column-parallel K2 with the output all-gather fused into the epilogue
    (multi-GPU inference, one process per GPU).  Rank `rank` of `world` holds
    weight rows [rank*n_loc, (rank+1)*n_loc) as B_local [n_loc, K] (scales and

@@ -285,6 +285,89 @@ def int8_gemm_block(a: np.ndarray, a_s: np.ndarray, b: np.ndarray, b_s: np.ndarr
     return acc.astype(np.float32)
 
 
+def _block_requant_trunc(y: np.ndarray, out_block_size: int) -> Tuple[np.ndarray, np.ndarray]:
+    """Per (row, ``out_block_size`` columns) requantization of the Triton
+    fused kernels (comfy/int8_kernels.py:755-767, 1200-1213):
+    ``scale = max(amax / 127, 1e-8)``, ``q = int8(clamp(y / scale, -127, 127))``
+    (fp32 division, conversion by truncation)."""
+    M, N = y.shape
+    assert N % out_block_size == 0
+    r = np.asarray(y, np.float32).reshape(M, N // out_block_size, out_block_size)
+    amax = np.abs(r).max(axis=2).astype(np.float32)
+    scale = np.maximum((amax / np.float32(127.0)).astype(np.float32), np.float32(1e-8)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        v = (r / scale[..., None]).astype(np.float32)
+    v = np.minimum(np.maximum(v, np.float32(-127.0)), np.float32(127.0))
+    return _trunc_i8(v).reshape(M, N), scale
+
+
+def int8_gemm_quant(a: np.ndarray, a_s: np.ndarray, b: np.ndarray, b_s: np.ndarray,
+                    bias: Optional[np.ndarray] = None, out_block_size: int = 128, block_size: int = 128,
+                    b_layout: str = "tile") -> Tuple[np.ndarray, np.ndarray]:
+    """Fused GEMM + output quantization, ``int8_gemm_quant`` /
+    ``int8_addmm_quant`` (comfy/int8_kernels.py:684-797, 800-917, 920-1089):
+    the block-promoted fp32 accumulator of :func:`int8_gemm_block`
+    (``acc += fp32(A_kb B_kb^T) * a_s * b_s`` in K-block order), ``+ bias``,
+    then the per-(row, 128-column block) int8 requantization.  Returns
+    ``(q int8 [M, N], scale float32 [M, N / out_block_size])``."""
+    acc = int8_gemm_block(a, a_s, b, b_s, bias, block_size, b_layout)
+    return _block_requant_trunc(acc, out_block_size)
+
+
+def _erf_f32(x: np.ndarray) -> np.ndarray:
+    """erf of float32 inputs evaluated in double and rounded to float32 (the
+    reference's Triton ``tl.math.erf`` as executed: math.erf per element)."""
+    xd = np.asarray(x, dtype=np.float64)
+    try:
+        from scipy.special import erf as _erf
+        return _erf(xd).astype(np.float32)
+    except ImportError:  # pragma: no cover
+        return np.vectorize(math.erf)(xd).astype(np.float32)
+
+
+def int8_gelu(q: np.ndarray, s: np.ndarray, block_size: int = 128) -> Tuple[np.ndarray, np.ndarray]:
+    """Fused int8 GELU, ``int8_gelu_kernel`` (comfy/int8_kernels.py:1122-1213):
+    ``v = fp32(q) * s`` per (row, block); ``e = erf(v / fp32(1.41421356237))``;
+    ``g = (v * 0.5) * (1 + e)`` (all fp32, left to right); then the same
+    per-(row, block) requantization as the fused GEMM.  Returns
+    ``(q int8 [M, N], scale float32 [M, N / block_size])``."""
+    M, N = q.shape
+    v = (q.astype(np.float32).reshape(M, N // block_size, block_size)
+         * np.asarray(s, np.float32).reshape(M, N // block_size)[..., None]).astype(np.float32)
+    e = _erf_f32((v / np.float32(1.41421356237)).astype(np.float32))
+    g = ((v * np.float32(0.5)).astype(np.float32) * (np.float32(1.0) + e).astype(np.float32)).astype(np.float32)
+    return _block_requant_trunc(g.reshape(M, N), block_size)
+
+
+def gptq_quant_block(w: np.ndarray, hinv: np.ndarray, scale) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """GPTQ / LDLQ error-feedback quantization of one column block,
+    ``gptq_quant_block_kernel`` (comfy/gptq_kernels.py:11-85), every row in
+    parallel.  ``w`` [M, B] fp32 (returned updated, as the kernel updates it in
+    place), ``hinv`` [B, B] fp32, ``scale`` a scalar or [M, 1].  For each column
+    j in order: ``s = max(|scale|, 1e-12)``, ``q = clamp(rint(w_j / s), -127, 127)``
+    (the kernel's floor/fraction test is round-half-even), ``d = max(|hinv[j, j]|,
+    1e-12)``, ``err = (w_j - q * s) / d``, then ``w_k -= err * hinv[j, k]`` for
+    k > j (fp32, separately rounded).  Returns ``(q int8 [M, B], err fp32 [M, B],
+    w fp32 [M, B])``."""
+    W = np.array(w, dtype=np.float32, copy=True)
+    H = np.asarray(hinv, dtype=np.float32)
+    M, B = W.shape
+    sc = np.asarray(scale, dtype=np.float32).reshape(-1)
+    sc = np.maximum(np.abs(sc if sc.size > 1 else np.full(M, sc[0], np.float32)), np.float32(1e-12))
+    Q = np.zeros((M, B), np.int8)
+    E = np.zeros((M, B), np.float32)
+    for j in range(B):
+        wj = W[:, j].copy()
+        q = np.clip(np.rint((wj / sc).astype(np.float32)), np.float32(-127.0), np.float32(127.0)).astype(np.float32)
+        Q[:, j] = q.astype(np.int8)
+        d = np.maximum(np.abs(H[j, j]), np.float32(1e-12)).astype(np.float32)
+        err = ((wj - (q * sc).astype(np.float32)).astype(np.float32) / d).astype(np.float32)
+        E[:, j] = err
+        if j + 1 < B:
+            W[:, j + 1:] = (W[:, j + 1:] - (err[:, None] * H[j, j + 1:][None, :]).astype(np.float32)).astype(np.float32)
+    return Q, E, W
+
+
 def gelu_f32(x: np.ndarray) -> np.ndarray:
     """Exact-erf GELU ``0.5 x (1 + erf(x / sqrt 2))`` (torch ``F.gelu`` default)."""
     xf = np.asarray(x, dtype=np.float64)

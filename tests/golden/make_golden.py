@@ -229,6 +229,69 @@ def main():
         qd.update({f"{tag}_w": wd, f"{tag}_q": res[0], f"{tag}_s": res[1], f"{tag}_deq": res[2]})
     save("quip_convert_defaults.npz", **qd)
 
+    # ---------------- checkpoint format: the reference's convert_to_int8 output
+    # for a tiny model (QuIP optimizer, comfy_quant metadata) in per-row
+    # tensorwise, block and store-transformed modes (its --simple mode: no bias
+    # correction from synthetic calibration data)
+    import tempfile
+    from safetensors.torch import save_file, load_file
+    from convert_to_quant.quantization import convert_to_int8
+    ck = {}
+    gck = gen(210)
+    model = {"blk.0.qkv.weight": (torch.randn(256, 128, generator=gck) * 0.02).to(torch.bfloat16),
+             "blk.0.qkv.bias": (torch.randn(256, generator=gck) * 0.01).to(torch.bfloat16),
+             "blk.0.proj.weight": (torch.randn(96, 192, generator=gck) * 0.02).to(torch.bfloat16),
+             "norm.weight": torch.ones(128, dtype=torch.bfloat16)}
+
+    def put(prefix, tensors):
+        names = sorted(tensors)
+        ck[f"{prefix}__keys"] = np.array(names)
+        ck[f"{prefix}__dtypes"] = np.array([str(tensors[k].dtype).replace("torch.", "") for k in names])
+        for k in names:
+            v = tensors[k]
+            ck[f"{prefix}/{k}"] = bits(v) if v.dtype == torch.bfloat16 else v.numpy()
+
+    put("in", model)
+    with tempfile.TemporaryDirectory() as td:
+        src = os.path.join(td, "in.safetensors")
+        save_file(model, src)
+        for tag, kw in (("tw", {}), ("blk", {"quip_requant_scheme": "block"}),
+                        ("st", {"quip_store_transformed": True})):
+            dst = os.path.join(td, f"out_{tag}.safetensors")
+            convert_to_int8(src, dst, comfy_quant=True, filter_flags={}, calib_samples=8, seed=0, optimizer="quip",
+                            no_learned_rounding=True, quip_seed=7, quip_actorder=False, **kw)
+            put(tag, load_file(dst))
+    save("ckpt_quip.npz", **ck)
+
+    # ------------- fused output requantization (interpreted Triton kernels)
+    xf = torch.randn(200, 384, generator=gen(200))
+    xf[:, 7] *= 25.0
+    fq, fs = IK.act_quant(xf)
+    wf = torch.randn(256, 384, generator=gen(201)) * 0.02
+    wq_, ws_ = IK.weight_quant(wf)
+    bias_f = torch.randn(256, generator=gen(202)) * 0.1
+    cq, cs = IK.int8_gemm_quant(fq, fs, wq_, ws_)
+    cqb, csb = IK.int8_addmm_quant(fq, fs, wq_, ws_, bias_f)
+    gx = torch.randn(150, 512, generator=gen(203)) * 2.0
+    gq, gs = IK.act_quant(gx)
+    oq, os_ = IK.int8_gelu(gq, gs)
+    save("gemm_quant.npz", aq=fq, a_s=fs, bq=wq_, b_s=ws_, bias=bias_f, c_q=cq, c_s=cs, cb_q=cqb, cb_s=csb,
+         g_in_q=gq, g_in_s=gs, g_q=oq, g_s=os_)
+
+    # -------------- GPTQ block kernel (interpreted Triton; one program per row)
+    from convert_to_quant.comfy import gptq_kernels as GK
+    gptq = {}
+    wg = torch.randn(24, 64, generator=gen(220)) * 0.02
+    xg = torch.randn(256, 64, generator=gen(221))
+    hg = xg.t() @ xg / 256 + 0.01 * torch.eye(64)
+    hinv = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(hg)), upper=True).contiguous()
+    for tag, sc in (("row", (wg.abs().amax(dim=1, keepdim=True) / 127).clamp(min=1e-8)),
+                    ("scalar", torch.tensor([float(wg.abs().max() / 127)]))):
+        w_run = wg.clone()
+        q_, e_ = GK.triton_gptq_quant_block(w_run, hinv, sc)
+        gptq.update({f"{tag}_scale": sc, f"{tag}_q": q_, f"{tag}_err": e_, f"{tag}_w_out": w_run})
+    save("gptq_block.npz", w=wg, hinv=hinv, **gptq)
+
     # ---------------------- transformed-space matmul (interpreted kernel)
     xq = torch.randn(16, 256, generator=gen(190))
     Qt = torch.randint(-127, 128, (128, 256), dtype=torch.int8, generator=gen(191))

@@ -23,7 +23,11 @@ def _unsplit(a, b, a_s, a_kind, b_s, b_kind, bias, dtype, act):
     return out
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (300, 512, 2048), (129, 1024, 8192)])
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (300, 512, 2048), (129, 1024, 8192),
+                                   # rows <= 128 take the CTA-pair kernel when they split (zero-filled rows)
+                                   (64, 3072, 12288), (37, 1024, 4096), (1, 512, 2048),
+                                   # per-rank shapes of the Flux stack split over 8 GPUs
+                                   (576, 3072, 15360), (512, 3072, 12288)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("kind", ["row", "scalar"])
 def test_split_k_equals_unsplit(M, N, K, dtype, kind):
@@ -54,7 +58,7 @@ def test_split_k_int32_equals_oracle():
     assert np.array_equal(got.cpu().numpy(), O.int_mm(a, b))
 
 
-def test_no_split_for_large_grids_or_block_scales():
+def test_split_decision_by_grid_and_scales():
     assert ops._gemm_ws_bytes(4096, 12288, 3072, L.QI8_S_ROW, L.QI8_S_ROW) == 0
     assert ops._gemm_ws_bytes(512, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW_KBLOCK) == 0
-    assert ops._gemm_ws_bytes(64, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW) == 0  # 1-CTA kernel rows
+    assert ops._gemm_ws_bytes(64, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW) > 0  # few rows, few tiles: splits

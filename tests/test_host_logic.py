@@ -110,3 +110,12 @@ def test_converter_keeps_reference_defaults_and_refuses_them():
     with pytest.raises(NotImplementedError, match="actorder"):
         QuIPInt8Converter()
     QuIPInt8Converter(**HADAMARD_RTN)
+
+
+def test_conversion_driver_selects_2d_weights_and_names_shards():
+    from convert_to_quant_quip_int8_b200 import convert as C
+    shapes = {"a.weight": (8, 16), "a.bias": (8,), "norm.weight": (16,), "b.lora_A.weight": (4, 16),
+              "c.weight": (32, 8), "emb": (10, 4)}
+    assert C.weight_keys(shapes) == ["a.weight", "b.lora_A.weight", "c.weight"]
+    assert C.weight_keys(shapes, exclude=lambda k: "lora" in k) == ["a.weight", "c.weight"]
+    assert C.shard_path("/x/m.safetensors", 1, 4) == "/x/m.safetensors.rank1-of-4"

@@ -180,3 +180,26 @@ def test_oracle_rotation_round_trip():
     sv = (r.integers(0, 2, 64) * 2 - 1).astype(np.float32)
     back = O.quip_inverse_rotate(O.quip_rotate_weight(w, su, sv), su, sv, 100, 60)
     assert np.max(np.abs(back - w)) < 1e-6
+
+
+def test_fused_requant_gemm_and_int8_gelu_golden(golden):
+    """int8_gemm_quant / int8_addmm_quant / int8_gelu (comfy/int8_kernels.py:
+    684-1089, 1122-1312), executed by the reference under the Triton
+    interpreter: int8 outputs and block scales bit-exact."""
+    g = golden("gemm_quant.npz")
+    q, s = O.int8_gemm_quant(g["aq"], g["a_s"], g["bq"], g["b_s"])
+    assert np.array_equal(q, g["c_q"]) and np.array_equal(s, g["c_s"])
+    q, s = O.int8_gemm_quant(g["aq"], g["a_s"], g["bq"], g["b_s"], g["bias"])
+    assert np.array_equal(q, g["cb_q"]) and np.array_equal(s, g["cb_s"])
+    q, s = O.int8_gelu(g["g_in_q"], g["g_in_s"])
+    assert np.array_equal(q, g["g_q"]) and np.array_equal(s, g["g_s"])
+
+
+def test_gptq_block_golden(golden):
+    """gptq_quant_block_kernel (comfy/gptq_kernels.py:11-85) under the Triton
+    interpreter: int8 codes, errors and the updated weight block bit-exact."""
+    g = golden("gptq_block.npz")
+    for tag in ("row", "scalar"):
+        q, e, w = O.gptq_quant_block(g["w"], g["hinv"], g[f"{tag}_scale"])
+        assert np.array_equal(q, g[f"{tag}_q"]) and np.array_equal(e, g[f"{tag}_err"])
+        assert np.array_equal(w, g[f"{tag}_w_out"])
