@@ -52,11 +52,13 @@ REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 # dominant kernel of each workload, from one ncu capture of that launch:
 #   ncu --clock-control none --metrics dram__bytes_read.sum,dram__bytes_write.sum \
 #       -k regex:gemm_pair_kernel -c 1 python benchmarks/microbench.py gemm_stack --profile --iters 1
-# (flux: the single-block linear1 GEMM, 4608 x 3072 -> 21504, per-row scales).
+# (flux: the single-block linear1 GEMM, 4608 x 3072 -> 21504, per-row scales; t5: with -s 3, the
+# wi GEMM, 4096 x 4096 -> 10240).
 PROFILED_TRAFFIC = {
     "flux": 81274624 + 145703424,  # read + write; 80 MB of operands, 198 MB of bf16 output (part stays in L2)
-    "t5": None,
-    "dit_mlp": None,
+    "t5": 59306496 + 35874816,  # one wi GEMM launch, 4096 x 4096 -> 10240 (operands 58.7 MB, output 84 MB)
+    # mean of the W1 and W2 block GEMM launches of the DiT pair (ncu --set full capture of both)
+    "dit_mlp": 128480000,
 }
 
 
@@ -957,6 +959,10 @@ def main_conversion(args):
         return
     hbm, hbm_note = hbm_peak()
     min_bytes = 4 * my_params  # bf16 read + int8 per-row + int8 block writes
+
+    def launches(m):  # column passes (one up to 2^9 rows, else two) forward and inverse, row pass, two requants
+        col = 1 if (1 << (m - 1).bit_length()) <= 512 else 2
+        return 2 * col + 3
     achieved = min_bytes / (ms / steps / 1e3) / 1e9
     line = {
         "metric": "QuIP conversion sweep tensors/s (304 tensors, 12.9 B params)", "value": round(value, 2),
@@ -976,7 +982,7 @@ def main_conversion(args):
                      "algorithmic": "4 B per parameter (bf16 read, int8 per-row and int8 block writes)",
                      "kernel": "whole conversion step (column/row FWHT passes, RTN, inverse, requants)",
                      "peak_note": hbm_note},
-        "gpu_launches": None, "clocks": clocks,
+        "gpu_launches": steps * sum(launches(shapes[i][0]) for i in mine), "clocks": clocks,
     }
     if not args.no_cpu_baseline and world == 1:
         v, unit, sec, threads, kind, sample = cpu_point("conversion")

@@ -414,6 +414,21 @@ __global__ void __launch_bounds__(1 << (L - 4), 1024 >> (L - 4)) rot2_kernel(Rot
     }
   };
   if (pre) fetch(blockIdx.x);
+  // the signs are per column: this thread's 16 are loaded once for all its rows
+  float sg[16];
+  if (a.pre_sign) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.pre_sign + c0) + q);
+      sg[4 * q] = s4.x; sg[4 * q + 1] = s4.y; sg[4 * q + 2] = s4.z; sg[4 * q + 3] = s4.w;
+    }
+  }
+  // For even L the normalization 1/sqrt(n) = 2^(-L/2) scales exactly, so in
+  // the per-token path it is folded into the amax and the reciprocal:
+  // rint(fl(fl(v * 2^-k) * rcp)) == rint(fl(v * (rcp * 2^-k))) and
+  // amax(fl(v * 2^-k)) == amax(v) * 2^-k, barring subnormal intermediates,
+  // which the row's amax test below sends to the unfolded path.
+  constexpr bool POW2_NORM = (L % 2) == 0;
   int it = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
     // a row's first write to its buffer follows the first barrier of the
@@ -432,17 +447,12 @@ __global__ void __launch_bounds__(1 << (L - 4), 1024 >> (L - 4)) rot2_kernel(Rot
     }
     if (a.pre_sign) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.pre_sign + c0) + q);
-        v[4 * q] = __fmul_rn(v[4 * q], s4.x);
-        v[4 * q + 1] = __fmul_rn(v[4 * q + 1], s4.y);
-        v[4 * q + 2] = __fmul_rn(v[4 * q + 2], s4.z);
-        v[4 * q + 3] = __fmul_rn(v[4 * q + 3], s4.w);
-      }
+      for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], sg[e]);
     }
     stages<L, 0>(v);
     phase<L, 1>(v, buf, t);
-    if (a.do_norm) {
+    const bool fold = OUT == RO_Q_TOKEN && POW2_NORM && a.do_norm;
+    if (a.do_norm && !fold) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], a.norm);
     }
@@ -456,8 +466,20 @@ __global__ void __launch_bounds__(1 << (L - 4), 1024 >> (L - 4)) rot2_kernel(Rot
       float amax = red[it & 1][0];
 #pragma unroll 1
       for (int w = 1; w < P / 32; ++w) amax = fmaxf(amax, red[it & 1][w]);
+      float nrm = 1.0f;
+      if (fold) {
+        amax = __fmul_rn(amax, a.norm);
+        // 2^-100 <= amax <= 2^100: a subnormal fl(v * 2^-k) quantizes to 0 on
+        // both paths and rcp * 2^-k stays normal
+        if (amax >= 7.8886091e-31f && amax <= 1.2676506e30f) {
+          nrm = a.norm;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], a.norm);
+        }
+      }
       const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
-      const float rcp = __frcp_rn(s);
+      const float rcp = __fmul_rn(__frcp_rn(s), nrm);
       // one byte per element in the last window's mapping: a warp writes 32
       // consecutive bytes per element index
       int8_t* qrow = a.q + row * N + wbase(t, WL);

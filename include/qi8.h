@@ -287,6 +287,20 @@ QI8_API int qi8_gemm_i8_quant(const int8_t* A, const int8_t* B, int64_t M, int64
 QI8_API int qi8_int8_gelu(const int8_t* q, const float* scale, int64_t rows, int64_t n, int block, int8_t* q_out,
                           float* scale_out, void* stream);
 
+/* GPTQ / LDLQ error-feedback quantization of one column block (replaces
+   gptq_quant_block_kernel / triton_gptq_quant_block, comfy/gptq_kernels.py:
+   11-124, called by converters/gptq_int8.py:137 and
+   converters/quip_int8.py:861-864).  W [M, B] fp32 (row stride ld_w, updated
+   in place), hinv [B, B] fp32 (row stride ld_h), scale: one fp32 value when
+   scale_is_scalar, else [M].  Per row, columns in order:
+   q = clamp(rint(w / s), -127, 127), e = (w - q s) / max(|hinv[j,j]|, 1e-12),
+   w_k -= e * hinv[j, k] for k > j (s = max(|scale|, 1e-12)), fp32, each
+   operation rounded separately.  q_out [M, B] int8, err_out [M, B] fp32;
+   B <= 128. */
+QI8_API int qi8_gptq_quant_block(float* W, int64_t M, int64_t B, int64_t ld_w, const float* hinv, int64_t ld_h,
+                                 const float* scale, int scale_is_scalar, int8_t* q_out, int64_t ld_q, float* err_out,
+                                 int64_t ld_e, void* stream);
+
 /* Column-parallel K2 with the output all-gather fused into the epilogue
    (multi-GPU inference, one process per GPU).  Rank `rank` of `world` holds
    weight rows [rank*n_loc, (rank+1)*n_loc) as B_local [n_loc, K] (scales and
