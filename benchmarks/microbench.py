@@ -126,6 +126,22 @@ def gemm_stack_cases(run, dev):
     return res
 
 
+def gemm_tile_cases(run, dev):
+    """The comfy block-wise layout's GEMM: per-(token, 128-K block)
+    activation scales x 128 x 128 weight-tile scales, bias, fp16 out."""
+    res = {}
+    M, N, K = 4096, 12288, 3072
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+    sa = torch.rand(M, K // 128, device=dev) * 0.01
+    sb = torch.rand(N // 128, K // 128, device=dev) * 0.01
+    bias = torch.randn(N, device=dev)
+    out = torch.empty(M, N, dtype=torch.float16, device=dev)
+    us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW_KBLOCK, sb, L.QI8_S_TILE128, bias, torch.float16, out=out))
+    res[f"k2_tile_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+    return res
+
+
 def convert_cases(run, dev):
     res = {}
     for M, N in [(3072, 3072), (12288, 3072), (3072, 12288)]:
@@ -139,6 +155,7 @@ def convert_cases(run, dev):
 
 
 CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "gemm_stack": gemm_stack_cases,
+         "gemm_tile": gemm_tile_cases,
          "convert": convert_cases}
 
 

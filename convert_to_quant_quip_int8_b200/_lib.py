@@ -72,6 +72,15 @@ SIGNATURES = {
     "qi8_gemm_i8_quant": (_I, [_P, _P, _I64, _I64, _I64, _P, _I, _P, _I, _P, _I, _P, _I64, _P, _I, _P]),
     "qi8_int8_gelu": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _P]),
     "qi8_gptq_quant_block": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I, _P, _I64, _P, _I64, _P]),
+    "qi8_col_sumsq": (_I, [_P, _I, _I64, _I64, _I64, _P, _P]),
+    "qi8_scale2d": (_I, [_P, _I, _I64, _I64, _I64, _P, _P, _I, _P, _I64, _P]),
+    "qi8_ldlq_prepare": (_I, [_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P]),
+    "qi8_hinv_workspace_bytes": (_I64, [_I64]),
+    "qi8_hinv_upper": (_I, [_P, _I64, _P, _P, _P, _I64, _P]),
+    "qi8_eye_f32": (_I, [_P, _I64, _P]),
+    "qi8_ldlq_workspace_bytes": (_I64, [_I64, _I64, _I]),
+    "qi8_ldlq": (_I, [_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _P]),
+    "qi8_ldlq_finish": (_I, [_P, _I64, _I64, _P, _P, _P, _P, _P]),
     "qi8_ipc_handle": (_I, [_P, _P, ctypes.POINTER(_I64)]),
     "qi8_ipc_open": (_I, [_P, _I64, ctypes.POINTER(_P)]),
     "qi8_ipc_close": (_I, [_P, _I64]),

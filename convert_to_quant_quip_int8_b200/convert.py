@@ -6,7 +6,10 @@ This is the QuIP branch of the reference's ``convert_to_int8``
 
 * weight selection: every 2-D tensor whose key ends in ``.weight``
   (quantization.py:364-372), minus an optional exclusion predicate;
-* per weight: ``QuIPInt8Converter(...).convert`` (Hadamard/RTN path, signs
+* per weight: ``QuIPInt8Converter(...).convert`` constructed as the
+  reference's driver constructs it (quantization.py:590-607: act-order from
+  ``quip_actorder``, diagonal rescaling and random permutation at their
+  defaults, ``H=None`` without calibration data; signs and permutation
   seeded by ``quip_seed`` and drawn on the CPU exactly as the reference),
   then the per-layer tensors with the reference's names and dtypes
   (quantization.py:651-727): ``weight`` int8, ``weight_scale`` fp32,
@@ -19,12 +22,9 @@ This is the QuIP branch of the reference's ``convert_to_int8``
   request (:773-776).
 
 Calibration data, SmoothQuant, learned rounding, LoRA merging and the
-reference's other optimizers are not part of this path.  The reference
-constructs its QuIP converter with diagonal rescaling and random permutation
-left at their defaults (quantization.py:590-607); this driver runs the
-Hadamard/RTN path without them, so tensor names, dtypes, shapes, metadata and
-sign vectors match the reference's output while the int8 values are those of
-the Hadamard/RTN path.
+reference's other optimizers are not part of this path (the reference's
+``--simple`` QuIP conversion: no bias correction from synthetic
+calibration data).
 
 Multi-GPU: weights are independent units.  ``rank`` of ``world`` converts its
 longest-processing-time share (``sharding.plan_partition`` on the padded
@@ -44,7 +44,7 @@ from typing import Callable, Dict, List, Optional
 
 import torch
 
-from .converters.quip_int8 import HADAMARD_RTN, QuIPInt8Converter
+from .converters.quip_int8 import QuIPInt8Converter
 from .sharding import plan_partition
 from .utils import comfy_quant as CQ
 
@@ -62,7 +62,8 @@ def shard_path(output_file: str, rank: int, world: int) -> str:
 
 
 def convert_to_int8_quip(input_file: str, output_file: str, *, comfy_quant: bool = True,
-                         quip_seed: Optional[int] = None, quip_store_transformed: bool = False,
+                         quip_seed: Optional[int] = None, quip_actorder: bool = True,
+                         quip_store_transformed: bool = False,
                          quip_requant_scheme: str = "tensor", quip_requant_tensor_per_row: bool = True,
                          block_size: int = 128, save_quant_metadata: bool = False, device: Optional[str] = None,
                          rank: int = 0, world: int = 1, exclude: Optional[Callable[[str], bool]] = None) -> dict:
@@ -83,9 +84,9 @@ def convert_to_int8_quip(input_file: str, output_file: str, *, comfy_quant: bool
         wkeys = weight_keys(shapes, exclude)
         plan = plan_partition([shapes[k] for k in wkeys], world)[rank]
         mine = [wkeys[i] for i in plan]
-        conv = QuIPInt8Converter(block_size=block_size, device=str(dev), seed=quip_seed,
+        conv = QuIPInt8Converter(block_size=block_size, device=str(dev), seed=quip_seed, actorder=quip_actorder,
                                  store_transformed=quip_store_transformed, requant_scheme=quip_requant_scheme,
-                                 requant_tensor_use_per_row_scale=quip_requant_tensor_per_row, **HADAMARD_RTN)
+                                 requant_tensor_use_per_row_scale=quip_requant_tensor_per_row)
 
         def read(key):
             return f.get_tensor(key).pin_memory()

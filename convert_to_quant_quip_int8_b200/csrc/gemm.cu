@@ -884,25 +884,45 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool b_col = !SWAP && p.b_kind == QI8_S_ROW_KBLOCK;
         const bool b_tile = p.b_kind == QI8_S_TILE128;
         const bool exact = !SWAP && e.exact;
+        // the K-block scales of blocks kb and kb + 1, loaded two blocks ahead
+        auto ld_s = [&](int k) -> float {
+          if (k >= KB) return 0.0f;
+          if constexpr (SWAP) return row_ok ? __ldg(p.b_scale + (int64_t)rr * KB + k) : 0.0f;
+          return a_kb ? (row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + k) : 0.0f) : 1.0f;
+        };
+        auto ld_b = [&](int k) -> float {
+          if (!b_tile || SWAP) return 1.0f;
+          return (cols_ok && k < KB) ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + k) : 0.0f;
+        };
+        auto ld_c = [&](int k, int c) -> float {
+          const int n = cc0 + c * 32 + lane;
+          return (b_col && n < p.N && k < KB) ? __ldg(p.b_scale + (int64_t)n * KB + k) : 0.0f;
+        };
+        float ps1 = ld_s(0), ps2 = ld_s(1), pb1 = ld_b(0), pb2 = ld_b(1), pc1[4], pc2[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { pc1[c] = ld_c(0, c); pc2[c] = ld_c(1, c); }
         for (int kb = 0; kb < KB; ++kb, ++au) {
           const int buf = au & 1;
           float sk = 1.0f, ska = 1.0f, skb = 1.0f;
           if constexpr (SWAP) {
-            sk = row_ok ? __ldg(p.b_scale + (int64_t)rr * KB + kb) : 0.0f;
+            sk = ps1;
           } else {
-            if (a_kb) sk = ska = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
-            if (b_tile) skb = cols_ok ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f;
+            sk = ska = ps1;
+            skb = pb1;
             if (b_tile) sk = __fmul_rn(sk, skb);
             if (b_col) {
               __syncwarp();
 #pragma unroll
               for (int c = 0; c < 4; ++c) {
-                const int n = cc0 + c * 32 + lane;
-                my_kb[c * 32 + lane] = n < p.N ? __ldg(p.b_scale + (int64_t)n * KB + kb) : 0.0f;
+                my_kb[c * 32 + lane] = pc1[c];
+                pc1[c] = pc2[c];
+                pc2[c] = ld_c(kb + 2, c);
               }
               __syncwarp();
             }
           }
+          ps1 = ps2; ps2 = ld_s(kb + 2);
+          pb1 = pb2; pb2 = ld_b(kb + 2);
           const float2 sk2 = make_float2(sk, sk);
           if (!mbar_wait(tfull_bar(buf, half), (au >> 1) & 1, abort_flag, p.status, ST_GEMM_EPILOGUE, WAIT_LIMIT_NS)) {
             ok = false;
@@ -935,16 +955,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                   acc[col >> 1].x = __fadd_rn(acc[col >> 1].x, __fmul_rn(__fmul_rn(f0, ska), b0));
                   acc[col >> 1].y = __fadd_rn(acc[col >> 1].y, __fmul_rn(__fmul_rn(f1, ska), b1));
                 }
+              } else if (!SWAP && b_col) {
+                // per-column weight scales of this K block (shared memory)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                               __int2float_rn((int)rb[c & 1][2 * j + 1]));
+                  acc[col >> 1] = __ffma2_rn(f, __fmul2_rn(lds_f2(my_kb + col), sk2), acc[col >> 1]);
+                }
               } else {
+                // one scale for the thread's columns in this K block
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                   const int col = c * 32 + 2 * j;
                   // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
                   const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
                                                __int2float_rn((int)rb[c & 1][2 * j + 1]));
-                  float2 sc = sk2;
-                  if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
-                  acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                  acc[col >> 1] = __ffma2_rn(f, sk2, acc[col >> 1]);
                 }
               }
             }
@@ -1313,6 +1341,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           sk_n1 = row_ok ? __ldg(srow) : 0.0f;
           sk_n2 = (row_ok && KB > 1) ? __ldg(srow + 1) : 0.0f;
         }
+        // Not swapped: the activation's (row, K block) scale, the weight's
+        // 128-tile scale and (per-row K-block weights) this lane's four column
+        // scales of K blocks kb and kb + 1, loaded two K blocks ahead like the
+        // swapped path's.  Columns cc0 .. cc0 + 127 lie in one 128-tile.
+        auto ld_a = [&](int k) -> float {
+          if (!a_kb) return 1.0f;
+          return (row_ok && k < KB) ? __ldg(p.a_scale + (int64_t)rr * KB + k) : 0.0f;
+        };
+        auto ld_b = [&](int k) -> float {
+          if (!b_tile) return 1.0f;
+          return (cc0 < C && k < KB) ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + k) : 0.0f;
+        };
+        auto ld_c = [&](int k, int c) -> float {
+          const int n = cc0 + c * 32 + lane;
+          return (b_col && n < p.N && k < KB) ? __ldg(p.b_scale + (int64_t)n * KB + k) : 0.0f;
+        };
+        float pa1 = 1.0f, pa2 = 1.0f, pb1 = 1.0f, pb2 = 1.0f, pc1[4], pc2[4];
+        if constexpr (!SWAP) {
+          pa1 = ld_a(0); pa2 = ld_a(1);
+          pb1 = ld_b(0); pb2 = ld_b(1);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) { pc1[c] = ld_c(0, c); pc2[c] = ld_c(1, c); }
+        }
         for (int kb = 0; kb < KB; ++kb, ++au) {
           const int buf = au & 1;
           // scale of the first and of the second 64-column run
@@ -1322,20 +1373,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             sk_n1 = sk_n2;
             sk_n2 = (row_ok && kb + 2 < KB) ? __ldg(srow + kb + 2) : 0.0f;
           } else {
-            if (a_kb) sk0 = sk1 = ska = row_ok ? __ldg(p.a_scale + (int64_t)rr * KB + kb) : 0.0f;
-            if (b_tile) {
-              skb0 = cc0 < C ? __ldg(p.b_scale + (int64_t)(cc0 >> 7) * KB + kb) : 0.0f;
-              skb1 = cc1 < C ? __ldg(p.b_scale + (int64_t)(cc1 >> 7) * KB + kb) : 0.0f;
-              sk0 = __fmul_rn(sk0, skb0);
-              sk1 = __fmul_rn(sk1, skb1);
-            }
+            ska = pa1;
+            skb0 = skb1 = pb1;
+            sk0 = sk1 = b_tile ? __fmul_rn(ska, skb0) : ska;
+            pa1 = pa2; pa2 = ld_a(kb + 2);
+            pb1 = pb2; pb2 = ld_b(kb + 2);
             if (b_col) {
               __syncwarp();
 #pragma unroll
               for (int c = 0; c < 4; ++c) {
-                const int j = c * 32 + lane;
-                const int n = j < 64 ? cc0 + j : cc1 + j - 64;
-                my_kb[j] = n < p.N ? __ldg(p.b_scale + (int64_t)n * KB + kb) : 0.0f;
+                my_kb[c * 32 + lane] = pc1[c];
+                pc1[c] = pc2[c];
+                pc2[c] = ld_c(kb + 2, c);
               }
               __syncwarp();
             }
@@ -1372,16 +1421,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                   acc[col >> 1].x = __fadd_rn(acc[col >> 1].x, __fmul_rn(__fmul_rn(f0, ska), b0));
                   acc[col >> 1].y = __fadd_rn(acc[col >> 1].y, __fmul_rn(__fmul_rn(f1, ska), b1));
                 }
+              } else if (!SWAP && b_col) {
+                // per-column weight scales of this K block (shared memory)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int col = c * 32 + 2 * j;
+                  const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
+                                               __int2float_rn((int)rb[c & 1][2 * j + 1]));
+                  acc[col >> 1] = __ffma2_rn(f, __fmul2_rn(lds_f2(my_kb + col), sk2), acc[col >> 1]);
+                }
               } else {
+                // one scale for the thread's columns in this K block
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                   const int col = c * 32 + 2 * j;
                   // exact int32 -> fp32 (|p| <= 128*128*128 < 2^24)
                   const float2 f = make_float2(__int2float_rn((int)rb[c & 1][2 * j]),
                                                __int2float_rn((int)rb[c & 1][2 * j + 1]));
-                  float2 sc = sk2;
-                  if (!SWAP && b_col) sc = __fmul2_rn(lds_f2(my_kb + col), sk2);
-                  acc[col >> 1] = __ffma2_rn(f, sc, acc[col >> 1]);
+                  acc[col >> 1] = __ffma2_rn(f, sk2, acc[col >> 1]);
                 }
               }
             }

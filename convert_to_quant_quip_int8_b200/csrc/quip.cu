@@ -188,8 +188,72 @@ __global__ void __launch_bounds__(RotCfg<L>::THREADS) quip_row_kernel(RowArgs a)
   }
 }
 
+// Row pass for rows of 2^9..2^14 on the phased transform (16 elements per
+// thread, see fwht_row.cuh): forward FWHT, x norm, row amax, division RTN
+// (+-127), dequantize, one exchange back to the contiguous mapping, inverse
+// FWHT, x norm.  The same operations in the same order as quip_row_kernel.
+template <int L>
+__global__ void __launch_bounds__(1 << (L - 4)) quip_row_phased_kernel(RowArgs a) {
+  using namespace rowfwht;
+  constexpr int N = 1 << L, NW = nwin<L>(), WL = wstart<L>(NW - 1);
+  extern __shared__ float4 dyn_smem[];
+  float* buf = reinterpret_cast<float*>(dyn_smem);
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  float* xr = a.x + row * a.ld_x;
+  float v[16];
+  // contiguous mapping: this thread holds elements t*16 .. t*16 + 15
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 f = reinterpret_cast<const float4*>(xr + t * 16)[q];
+    v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+  }
+  stages<L, 0>(v);
+  phase<L, 1>(v, buf, t);
+  // last-window mapping: element e is index ib + (e << WL)
+  const int ib = wbase(t, WL);
+  float local = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    v[e] = __fmul_rn(v[e], a.norm);
+    local = fmaxf(local, fabsf(v[e]));
+  }
+  const float amax = block_max(local, red);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int8_t q = rint_clamp(__fdiv_rn(v[e], s), -127.0f, 127.0f);
+    if (a.q_rot) a.q_rot[row * N + ib + (e << WL)] = q;
+    v[e] = __fmul_rn((float)q, s);
+  }
+  if (a.s_rot && t == 0) a.s_rot[row] = s;
+  // back to the contiguous mapping (block_max above ordered every read of the
+  // last phase before these writes; each address is written by its reader)
+  {
+    const int sb = swz(ib);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) buf[sb ^ swz(e << WL)] = v[e];
+    __syncthreads();
+    const int sc = swz(t * 16);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = buf[sc ^ swz(e)];
+  }
+  stages<L, 0>(v);
+  phase<L, 1>(v, buf, t);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) xr[ib + (e << WL)] = __fmul_rn(v[e], a.norm);
+}
+
 template <int L>
 int launch_row_L(const RowArgs& a, int64_t rows, cudaStream_t st) {
+  if constexpr (L >= 9 && L <= 14) {
+    auto pk = quip_row_phased_kernel<L>;
+    constexpr int SM = (1 << L) * 4;
+    if (SM > 48 * 1024) QI8_CUDA(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, SM));
+    pk<<<(unsigned)rows, 1 << (L - 4), SM, st>>>(a);
+    return check_cuda(cudaGetLastError(), "quip_row_phased_kernel launch");
+  }
   using C = RotCfg<L>;
   auto kern = quip_row_kernel<L>;
   if (C::SMEM > 48 * 1024)

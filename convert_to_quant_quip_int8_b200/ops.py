@@ -376,6 +376,101 @@ def requant_weight(w: torch.Tensor, requant: int = L.QI8_REQ_ROW, block: int = 1
     return q, s
 
 
+# ---------------------------------------------------------------------------
+# QuIP with the reference's defaults (diagonal rescaling, random permutation,
+# damping, act-order, fp64 Hessian factorization, blocked LDLQ)
+# ---------------------------------------------------------------------------
+
+def col_sumsq(w: torch.Tensor) -> torch.Tensor:
+    """``(W ** 2).sum(dim=0)`` in fp32, summed in torch's CPU order
+    (converters/quip_int8.py:266)."""
+    L.require_cuda(w)
+    assert w.dim() == 2 and w.stride(1) == 1, "weight must be a row-major 2-D tensor"
+    M, N = w.shape
+    out = torch.empty(N, dtype=torch.float32, device=w.device)
+    L.check(L.load().qi8_col_sumsq(L.ptr(w), L.dtype_code(w.dtype), M, N, w.stride(0), L.ptr(out),
+                                   L.stream_ptr(w.device)), "qi8_col_sumsq")
+    return out
+
+
+def scale2d(x: Optional[torch.Tensor], shape: tuple, row: Optional[torch.Tensor] = None,
+            col: Optional[torch.Tensor] = None, divide: bool = False, device=None) -> torch.Tensor:
+    """``(x * col[None, :]) * row[:, None]`` or ``x / col[None, :]`` in fp32
+    (converters/quip_int8.py:280-285, 303); ``x=None`` is the identity."""
+    dev = x.device if x is not None else device
+    if x is not None:
+        L.require_cuda(x)
+        assert x.stride(1) == 1, "x must be row-major"
+    M, N = shape
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    L.check(L.load().qi8_scale2d(L.ptr(x), L.dtype_code(x.dtype) if x is not None else 0, M, N,
+                                 x.stride(0) if x is not None else N, L.ptr(row), L.ptr(col), int(bool(divide)),
+                                 L.ptr(out), N, L.stream_ptr(dev)), "qi8_scale2d")
+    return out
+
+
+def ldlq_prepare(w_rot: torch.Tensor, h_rot: torch.Tensor, cols: torch.Tensor, dead: torch.Tensor,
+                 diag: torch.Tensor):
+    """Gather W' and H' into LDLQ column order ``cols`` (dead columns zeroed,
+    damped diagonal ``diag``), the per-row scale, and the Hessian reversed
+    for the factorization.  Returns ``(W_p fp32 [M, N], scale [M, 1], H_rev fp64 [N, N])``."""
+    M, N = w_rot.shape
+    dev = w_rot.device
+    wp = torch.empty((M, N), dtype=torch.float32, device=dev)
+    sc = torch.empty((M, 1), dtype=torch.float32, device=dev)
+    hrev = torch.empty((N, N), dtype=torch.float64, device=dev)
+    L.check(L.load().qi8_ldlq_prepare(L.ptr(w_rot), L.ptr(h_rot), M, N, L.ptr(cols), L.ptr(dead), L.ptr(diag),
+                                      L.ptr(wp), L.ptr(sc), L.ptr(hrev), L.stream_ptr(dev)), "qi8_ldlq_prepare")
+    return wp, sc, hrev
+
+
+def hinv_upper(h_rev: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Upper Cholesky factor of H^-1 from the reversed damped Hessian (fp64,
+    overwritten); returns ``(U fp32 [N, N], info int32 device scalar)`` --
+    info != 0 marks a non-positive pivot (the reference then uses the
+    identity, converters/quip_int8.py:1211-1216)."""
+    N = h_rev.shape[0]
+    dev = h_rev.device
+    lib = L.load()
+    hinv = torch.empty((N, N), dtype=torch.float32, device=dev)
+    info = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.empty(int(lib.qi8_hinv_workspace_bytes(N)), dtype=torch.uint8, device=dev)
+    L.check(lib.qi8_hinv_upper(L.ptr(h_rev), N, L.ptr(hinv), L.ptr(info), L.ptr(ws), ws.numel(),
+                               L.stream_ptr(dev)), "qi8_hinv_upper")
+    return hinv, info
+
+
+def eye_f32(n: int, device) -> torch.Tensor:
+    out = torch.empty((n, n), dtype=torch.float32, device=device)
+    L.check(L.load().qi8_eye_f32(L.ptr(out), n, L.stream_ptr(device)), "qi8_eye_f32")
+    return out
+
+
+def ldlq(w: torch.Tensor, hinv: torch.Tensor, scale: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """The LDLQ pass (converters/quip_int8.py:813-945); ``w`` fp32 [M, N] is
+    consumed (updated in place).  Returns ``Q'`` int8 [M, N]."""
+    M, N = w.shape
+    dev = w.device
+    lib = L.load()
+    q = torch.empty((M, N), dtype=torch.int8, device=dev)
+    ws = torch.empty(int(lib.qi8_ldlq_workspace_bytes(M, N, block)), dtype=torch.uint8, device=dev)
+    L.check(lib.qi8_ldlq(L.ptr(w), M, N, L.ptr(hinv), L.ptr(scale), block, L.ptr(q), L.ptr(ws), ws.numel(),
+                         L.stream_ptr(dev)), "qi8_ldlq")
+    return q
+
+
+def ldlq_finish(q: torch.Tensor, scale: torch.Tensor, cols: torch.Tensor, want_deq: bool = True,
+                want_q: bool = False):
+    """Scatter LDLQ columns back to rotated order: ``(deq fp32 or None, q int8 or None)``."""
+    M, N = q.shape
+    dev = q.device
+    deq = torch.empty((M, N), dtype=torch.float32, device=dev) if want_deq else None
+    qs = torch.empty((M, N), dtype=torch.int8, device=dev) if want_q else None
+    L.check(L.load().qi8_ldlq_finish(L.ptr(q), M, N, L.ptr(scale), L.ptr(cols), L.ptr(deq), L.ptr(qs),
+                                     L.stream_ptr(dev)), "qi8_ldlq_finish")
+    return deq, qs
+
+
 def device_status(reset: bool = True) -> None:
     """Raise if a kernel's bounded wait expired since the last check."""
     L.check(L.load().qi8_device_status(int(reset)), "device status")

@@ -301,6 +301,71 @@ QI8_API int qi8_gptq_quant_block(float* W, int64_t M, int64_t B, int64_t ld_w, c
                                  const float* scale, int scale_is_scalar, int8_t* q_out, int64_t ld_q, float* err_out,
                                  int64_t ld_e, void* stream);
 
+/* ---- QuIP with the reference's default options (QuIPInt8Converter.convert,
+   converters/quip_int8.py:1031-1345: diagonal rescaling, random permutation,
+   damping, act-order, fp64 Hessian factorization, blocked LDLQ).  The
+   converter's host side computes the O(N) vectors between these steps
+   (D_tilde, the permutations, the damped diagonal). */
+
+/* out[j] = sum_i w[i, j]^2 in fp32, summed in torch's CPU order: columns in
+   groups of 32 (N >= 8; groups of 4 for N < 8) by a four-level cascade over
+   the rows, the remaining columns by the 4-lane row_sum (replaces
+   (W ** 2).sum(dim=0), converters/quip_int8.py:266).  w [M, N] bf16 / f16 /
+   f32, row stride ld_w. */
+QI8_API int qi8_col_sumsq(const void* w, int w_dtype, int64_t M, int64_t N, int64_t ld_w, float* out, void* stream);
+
+/* out[i, j] = divide ? x[i, j] / col_scale[j] : (x[i, j] * col_scale[j]) * row_scale[i]
+   (row_scale may be NULL; x == NULL is the identity, M == N): the rescaling
+   W * D, (H * Dinv_j) * Dinv_i and its undo W / D
+   (converters/quip_int8.py:280-285, 303).  out fp32, row stride ld_out. */
+QI8_API int qi8_scale2d(const void* x, int x_dtype, int64_t M, int64_t N, int64_t ld_x, const float* row_scale,
+                        const float* col_scale, int divide, float* out, int64_t ld_out, void* stream);
+
+/* LDLQ inputs in LDLQ column order (converters/quip_int8.py:336-340,
+   1105-1146, 1272-1274).  w_rot [M, N] and h_rot [N, N] fp32 are the rotated
+   weight and Hessian; LDLQ position j holds rotated column cols[j] (the
+   random permutation composed with act-order); dead[j] != 0 zeroes that
+   weight column; diag[j] is the damped diagonal at position j.  Outputs:
+   w_out [M, N] fp32, scale_out [M] = max(row amax / 127, 1e-12), and h_rev
+   [N, N] fp64 = J Hs J (lower triangle, zeros above), Hs being the damped
+   permuted Hessian symmetrized from its lower triangle.  N a power of two
+   <= 32768. */
+QI8_API int qi8_ldlq_prepare(const float* w_rot, const float* h_rot, int64_t M, int64_t N, const int32_t* cols,
+                             const uint8_t* dead, const float* diag, float* w_out, float* scale_out, double* h_rev,
+                             void* stream);
+
+/* hinv_out [N, N] fp32 = the upper Cholesky factor U of Hs^-1 (Hs^-1 = U^T U),
+   computed in fp64 from h_rev (overwritten) as J L^-1 J with L = chol(h_rev);
+   replaces chol -> cholesky_inverse -> chol(upper) (converters/quip_int8.py:
+   1195-1199).  *info (device int) is 0, or 1 + the index of the first
+   non-positive pivot (the reference then falls back to the identity,
+   :1211-1216).  workspace >= qi8_hinv_workspace_bytes(N), 16-byte aligned. */
+QI8_API int64_t qi8_hinv_workspace_bytes(int64_t N);
+QI8_API int qi8_hinv_upper(double* h_rev, int64_t N, float* hinv_out, int* info, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+
+/* out [N, N] fp32 = identity (the fallback Hinv of :1216). */
+QI8_API int qi8_eye_f32(float* out, int64_t N, void* stream);
+
+/* One LDLQ pass (replaces _single_ldlq_pass + _quantize_block_lazy,
+   converters/quip_int8.py:813-945, 638-672): for each `block` columns
+   (16..128, a multiple of 16), 16-column batches q = clamp(rint(w / s),
+   -127, 127), err = (w - q s) / max(hinv_jj, 1e-12), the rest of the block
+   updated by err @ hinv[batch, rest]; after the block every later column
+   by Err_block @ hinv[block, later].  Every dot product is accumulated by
+   fmaf in index order from zero, then subtracted (fp32).  w [M, N] fp32 is
+   consumed; scale [M]; q_out [M, N] int8.  workspace >=
+   qi8_ldlq_workspace_bytes(M, N, block). */
+QI8_API int64_t qi8_ldlq_workspace_bytes(int64_t M, int64_t N, int block);
+QI8_API int qi8_ldlq(float* w, int64_t M, int64_t N, const float* hinv, const float* scale, int block,
+                     int8_t* q_out, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Back to rotated column order (undo act-order and the random permutation,
+   converters/quip_int8.py:1348-1365, 1467-1474): deq_out[i, cols[j]] =
+   q[i, j] * scale[i] (fp32, :1452) and/or q_out[i, cols[j]] = q[i, j]. */
+QI8_API int qi8_ldlq_finish(const int8_t* q, int64_t M, int64_t N, const float* scale, const int32_t* cols,
+                            float* deq_out, int8_t* q_out, void* stream);
+
 /* Column-parallel K2 with the output all-gather fused into the epilogue
    (multi-GPU inference, one process per GPU).  Rank `rank` of `world` holds
    weight rows [rank*n_loc, (rank+1)*n_loc) as B_local [n_loc, K] (scales and

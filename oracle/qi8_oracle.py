@@ -533,6 +533,212 @@ def quip_convert(w: np.ndarray, s_u: np.ndarray, s_v: np.ndarray, requant_scheme
     return q, s, deq
 
 
+# --------------------------------------------------------------------------
+# QuIP with the reference's defaults: diagonal rescaling, random permutation,
+# damping, act-order, fp64 Hessian factorization, blocked lazy LDLQ
+# --------------------------------------------------------------------------
+
+def _cascade_rows(rows: np.ndarray) -> np.ndarray:
+    """torch's CPU ``multi_row_sum``: a four-level cascade down axis 0, every
+    trailing column independent.  Level 0 adds ``step = 2**max(4,
+    ceil_log2(size) // 4)`` rows in order, is added into level 1 and cleared;
+    level j carries into level j+1 whenever the row count is a multiple of
+    ``step**j``; left-over rows go into level 0; finally ``acc0 += acc1;
+    acc0 += acc2; acc0 += acc3``."""
+    size = rows.shape[0]
+    lp = max(4, (int(math.ceil(math.log2(size))) if size > 1 else 0) // 4)
+    step, mask = 1 << lp, (1 << lp) - 1
+    acc = [np.zeros(rows.shape[1:], np.float32) for _ in range(4)]
+    i = 0
+    while i + step <= size:
+        for _ in range(step):
+            acc[0] = (acc[0] + rows[i]).astype(np.float32)
+            i += 1
+        for j in range(1, 4):
+            acc[j] = (acc[j] + acc[j - 1]).astype(np.float32)
+            acc[j - 1] = np.zeros_like(acc[0])
+            if i & (mask << (j * lp)):
+                break
+    while i < size:
+        acc[0] = (acc[0] + rows[i]).astype(np.float32)
+        i += 1
+    for j in range(1, 4):
+        acc[0] = (acc[0] + acc[j]).astype(np.float32)
+    return acc[0]
+
+
+def _row_sum(cols: np.ndarray) -> np.ndarray:
+    """torch's CPU ``row_sum``: the M values of a column viewed as [M/4, 4],
+    a cascade (:func:`_cascade_rows`) per lane, the M % 4 left-over values
+    added to lane 0 in order, then ``lane0 += lane1; += lane2; += lane3``."""
+    M = cols.shape[0]
+    si = M // 4
+    if si:
+        p = _cascade_rows(cols[:si * 4].reshape(si, 4, *cols.shape[1:]))
+        lanes = [p[k].copy() for k in range(4)]
+    else:
+        lanes = [np.zeros(cols.shape[1:], np.float32) for _ in range(4)]
+    for i in range(si * 4, M):
+        lanes[0] = (lanes[0] + cols[i]).astype(np.float32)
+    for k in range(1, 4):
+        lanes[0] = (lanes[0] + lanes[k]).astype(np.float32)
+    return lanes[0]
+
+
+COLSUM_VEC = 8  # float lanes of the CPU sum kernel torch selects (AVX2 width)
+
+
+def col_sumsq(w: np.ndarray) -> np.ndarray:
+    """``(W ** 2).sum(dim=0)`` in fp32 with torch's CPU summation order
+    (converters/quip_int8.py:266).  With N >= 8 columns the reduction runs in
+    groups of 4 x 8 columns, each column a :func:`_cascade_rows` over the
+    rows, and the last ``N % 32`` columns by :func:`_row_sum`; with N < 8,
+    groups of 4 columns by the cascade and the last ``N % 4`` by
+    :func:`_row_sum`.  (The multi-threaded split keeps column chunks at
+    multiples of 32, so the grouping does not depend on the thread count.)"""
+    sq = (np.asarray(w, np.float32) * np.asarray(w, np.float32)).astype(np.float32)
+    N = sq.shape[1]
+    nv = (N // (4 * COLSUM_VEC)) * 4 * COLSUM_VEC if N >= COLSUM_VEC else (N // 4) * 4
+    out = np.zeros(N, np.float32)
+    if nv:
+        out[:nv] = _cascade_rows(sq[:, :nv])
+    if nv < N:
+        out[nv:] = _row_sum(sq[:, nv:])
+    return out
+
+
+def diag_rescale(w: np.ndarray, h: Optional[np.ndarray]):
+    """``_apply_diagonal_rescaling`` (converters/quip_int8.py:244-287):
+    ``D = clamp(float((max(diag H, 1e-12) / max(colsumsq, 1e-12)) ** 0.25), 0.1, 10)``
+    with the ratio and the fourth root in fp64; ``W * D`` per column and
+    ``(H * Dinv_j) * Dinv_i`` with ``Dinv = 1 / D`` (fp32).  ``h=None`` is the
+    identity Hessian.  Returns ``(W_r, H_r, D)``."""
+    w = np.asarray(w, np.float32)
+    N = w.shape[1]
+    hd = np.ones(N, np.float32) if h is None else np.diag(np.asarray(h, np.float32)).copy()
+    wtw = np.maximum(col_sumsq(w), np.float32(1e-12))
+    hd = np.maximum(hd, np.float32(1e-12))
+    D = np.power(hd.astype(np.float64) / wtw.astype(np.float64), 0.25).astype(np.float32)
+    D = np.clip(D, np.float32(0.1), np.float32(10.0)).astype(np.float32)
+    wr = (w * D[None, :]).astype(np.float32)
+    dinv = (np.float32(1.0) / D).astype(np.float32)
+    hm = np.eye(N, dtype=np.float32) if h is None else np.asarray(h, np.float32)
+    hr = ((hm * dinv[None, :]).astype(np.float32) * dinv[:, None]).astype(np.float32)
+    return wr, hr, D
+
+
+def ldlq_prepare(wrot: np.ndarray, hrot: np.ndarray, perm: np.ndarray, order: np.ndarray,
+                 percdamp: float = 0.01):
+    """Random permutation, dead-column handling, damping and act-order
+    (converters/quip_int8.py:336-340 with :1105-1146): ``W'[:, perm]``,
+    ``H'[perm][:, perm]``; ``dead = diag == 0`` gets ``H_ii = 1`` and a zero
+    weight column; ``damp = float32(percdamp) * float32(mean(diag, fp64))`` is
+    added to the diagonal; then the act-order permutation ``order`` (the
+    reference's ``argsort(diag(H), descending=True)``, computed by the caller
+    because its tie order is that of torch's unstable CPU sort).  Returns
+    ``(W_p fp32 [M, N], H_p fp64 [N, N], damp)``."""
+    W = np.asarray(wrot, np.float32)[:, perm].copy()
+    H = np.asarray(hrot, np.float32)[perm][:, perm].copy()
+    d = np.diag(H).copy()
+    dead = d == 0
+    idx = np.nonzero(dead)[0]
+    H[idx, idx] = 1.0
+    W[:, dead] = 0.0
+    damp = np.float32(np.float32(percdamp) * np.float32(np.mean(d.astype(np.float64))))
+    r = np.arange(H.shape[0])
+    H[r, r] = (H[r, r] + damp).astype(np.float32)
+    return W[:, order].copy(), H[order][:, order].astype(np.float64), damp
+
+
+def damped_order_keys(hrot: np.ndarray, perm: np.ndarray, percdamp: float = 0.01) -> np.ndarray:
+    """The damped diagonal the act-order sort ranks (converters/quip_int8.py:1105-1117)."""
+    d = np.diag(np.asarray(hrot, np.float32))[perm].copy()
+    damp = np.float32(np.float32(percdamp) * np.float32(np.mean(d.astype(np.float64))))
+    d = np.where(d == 0, np.float32(1.0), d).astype(np.float32)
+    return (d + damp).astype(np.float32)
+
+
+def ldlq_hinv(hp: np.ndarray) -> np.ndarray:
+    """``cholesky(cholesky_inverse(cholesky(H)), upper=True)`` in fp64, cast to
+    fp32 (converters/quip_int8.py:1195-1199): the upper Cholesky factor U of
+    H^-1 (``H^-1 = U^T U``)."""
+    L = np.linalg.cholesky(np.asarray(hp, np.float64))
+    Li = np.linalg.inv(L)
+    Hi = Li.T @ Li
+    return np.linalg.cholesky(Hi).T.astype(np.float32)
+
+
+def _fma_f32(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
+    """``fmaf(a, b, c)`` for fp32 arrays: the product is exact in fp64, the sum
+    is rounded to fp64 and then to fp32 (differs from one rounding only when
+    the fp64 sum lands exactly on an fp32 midpoint)."""
+    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(np.float32)
+
+
+def _dot_update(w: np.ndarray, err: np.ndarray, h: np.ndarray, order: str) -> np.ndarray:
+    """``w - err @ h`` (fp32).  ``order="blas"``: numpy's fp32 matmul (the
+    reference's torch CPU matmul, converters/quip_int8.py:667, 896-899);
+    ``order="seq"``: each dot product accumulated by fmaf in index order from
+    zero, then subtracted -- the device kernels' order."""
+    if order == "blas":
+        return (w - (err @ h).astype(np.float32)).astype(np.float32)
+    acc = np.zeros((err.shape[0], h.shape[1]), np.float32)
+    for k in range(err.shape[1]):
+        acc = _fma_f32(err[:, k:k + 1], h[k:k + 1, :], acc)
+    return (w - acc).astype(np.float32)
+
+
+def ldlq_pass(w: np.ndarray, hinv: np.ndarray, scale: np.ndarray, block: int = 128, batch: int = 16,
+              order: str = "blas") -> np.ndarray:
+    """One LDLQ pass, ``_single_ldlq_pass`` + ``_quantize_block_lazy``
+    (converters/quip_int8.py:813-945, 638-672): for each ``block`` columns, for
+    each ``batch`` of 16 columns quantize them together (``q = clamp(rint(w /
+    s), -127, 127)``, ``err = (w - q * s) / max(Hinv_jj, 1e-12)``), update the
+    rest of the block with ``err @ Hinv[batch, rest]``; after the block update
+    every later column with ``Err_block @ Hinv[block, later]``.  Rows are
+    independent.  Returns ``Q'`` int8."""
+    W = np.array(w, np.float32, copy=True)
+    H = np.asarray(hinv, np.float32)
+    s = np.asarray(scale, np.float32).reshape(-1, 1)
+    M, N = W.shape
+    Q = np.zeros((M, N), np.int8)
+    for i1 in range(0, N, block):
+        i2 = min(i1 + block, N)
+        E = np.zeros((M, i2 - i1), np.float32)
+        for j in range(i1, i2, batch):
+            e = min(j + batch, i2)
+            wb = W[:, j:e]
+            q = np.clip(np.rint((wb / s).astype(np.float32)), -127.0, 127.0).astype(np.float32)
+            Q[:, j:e] = q.astype(np.int8)
+            d = np.maximum(np.diag(H[j:e, j:e]), np.float32(1e-12)).astype(np.float32)
+            err = ((wb - (q * s).astype(np.float32)).astype(np.float32) / d[None, :]).astype(np.float32)
+            E[:, j - i1:e - i1] = err
+            if e < i2:
+                W[:, e:i2] = _dot_update(W[:, e:i2], err, H[j:e, e:i2], order)
+        if i2 < N:
+            W[:, i2:] = _dot_update(W[:, i2:], E, H[i1:i2, i2:], order)
+    return Q
+
+
+def quip_ldlq_scale(wp: np.ndarray) -> np.ndarray:
+    """``(amax_row / 127).clamp(min=1e-12)`` on the prepared W (converters/quip_int8.py:1272-1274)."""
+    return quip_rtn_rows(wp)[1]
+
+
+def quip_ldlq_finish(qp: np.ndarray, scale: np.ndarray, cols: np.ndarray, s_u: np.ndarray, s_v: np.ndarray,
+                     M: int, N: int, D: Optional[np.ndarray]):
+    """Undo act-order and the random permutation (``cols[j]`` is the rotated
+    column held at LDLQ position j), dequantize ``Q' * scale``, inverse
+    rotation, slice and ``W / D`` (converters/quip_int8.py:1348-1365, 1452,
+    1467-1513).  Returns ``(Q' in rotated column order, dequantized W)``."""
+    qo = np.zeros_like(qp)
+    qo[:, cols] = qp
+    deq = quip_unrotate_weight(qo, scale, s_u, s_v, M, N)
+    if D is not None:
+        deq = (deq / np.maximum(np.asarray(D, np.float32), np.float32(1e-12))[None, :]).astype(np.float32)
+    return qo, deq
+
+
 def lpt_partition(costs, n_parts: int):
     """Longest-processing-time-first assignment of units to ``n_parts`` bins.
 

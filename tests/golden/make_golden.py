@@ -59,8 +59,13 @@ def main():
                     required="QI8_REFERENCE_PATH" not in os.environ,
                     help="checkout of convert_to_quant (the directory holding the convert_to_quant package); "
                          "defaults to $QI8_REFERENCE_PATH")
+    ap.add_argument("--only", choices=["ldlq"], default=None,
+                    help="regenerate only this fixture (quip_ldlq.npz)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
+    if args.only == "ldlq":
+        make_ldlq()
+        return
 
     from convert_to_quant.utils import hadamard as H
     from convert_to_quant.utils.float_utils import quantize_int8_axiswise, quantize_int8_tensorwise
@@ -300,6 +305,73 @@ def main():
     sv = torch.randint(0, 2, (256,), generator=gen(194)).float() * 2 - 1
     yq = IK.quip_int8_matmul(xq, Qt, st_, su, sv)
     save("quip_matmul.npz", x=xq, Q=Qt, scale=st_, s_u=su, s_v=sv, y=yq)
+
+    make_ldlq()
+
+
+def make_ldlq():
+    """The reference converter with its defaults (diagonal rescaling, random
+    permutation, act-order, damping, fp64 Hessian factorization, blocked LDLQ),
+    with the intermediate tensors recorded by wrapping two of its methods:
+    ``_apply_incoherence`` (rescaled + rotated + permuted W and H, the signs,
+    D_tilde and the random permutation) and ``_ldlq_with_iterations`` (the
+    damped, act-order-permuted W, the fp32 upper Cholesky factor of H^-1 and
+    the per-row scale it is given, and the Q' it returns).  The act-order
+    permutation is recomputed here with the reference's own call on the damped
+    diagonal.  Cases: identity Hessian at two padded widths (one block-aligned
+    multi-block case) and one calibrated Hessian; per-row, block and
+    store-transformed outputs."""
+    from convert_to_quant.converters.quip_int8 import QuIPInt8Converter
+
+    out = {}
+    cases = (("id", (96, 192), None, {}),
+             ("wide", (40, 600), None, {}),
+             ("cal", (64, 160), 520, {}),
+             ("blk", (96, 256), None, {"requant_scheme": "block"}),
+             ("st", (80, 192), 521, {"store_transformed": True}))
+    for i, (tag, shape, hseed, kw) in enumerate(cases):
+        w = torch.randn(*shape, generator=gen(500 + i)) * 0.02
+        w[:, 3] *= 8.0  # one outlier column, so the rescaling is not uniform
+        H = None
+        if hseed is not None:
+            X = torch.randn(4 * shape[1], shape[1], generator=gen(hseed))
+            X[:, 5] *= 4.0
+            H = (X.t() @ X) / X.shape[0]
+        conv = QuIPInt8Converter(device="cpu", seed=11, **kw)
+        rec = {}
+        inc, ldlq = conv._apply_incoherence, conv._ldlq_with_iterations
+
+        def inc_hook(W_, H_, _f=inc, _r=rec):
+            r = _f(W_, H_)
+            _r.update(Wrot=r[0].clone(), Hrot=r[1].clone(), s_u=r[4], s_v=r[5],
+                      D=r[6] if r[6] is not None else torch.ones(0), perm=r[7])
+            return r
+
+        def ldlq_hook(W_, Hinv_, scale_, iterations=1, _f=ldlq, _r=rec):
+            _r.update(Wldlq=W_.clone(), Hinv=Hinv_.clone(), scale=scale_.clone())
+            q = _f(W_, Hinv_, scale_, iterations=iterations)
+            _r.update(Qldlq=q.clone())
+            return q
+
+        conv._apply_incoherence, conv._ldlq_with_iterations = inc_hook, ldlq_hook
+        res = conv.convert(w.clone(), None if H is None else H.clone())
+        # the act-order permutation, recomputed with the reference's own call
+        Hd = rec["Hrot"].clone()
+        diag = torch.diag(Hd)
+        dead = diag == 0
+        Hd[dead, dead] = 1
+        damp = conv.percdamp * torch.mean(diag.double()).float()
+        idx = torch.arange(Hd.shape[0])
+        Hd[idx, idx] += damp
+        order = torch.argsort(torch.diag(Hd), descending=True)
+        for k in ("Hrot", "Wrot") if tag in ("id", "cal") else ("Hrot", "Hinv", "Wrot"):
+            rec.pop(k)  # recomputable from pinned steps; Hinv kept for two cases
+        out.update({f"{tag}_{k}": v for k, v in rec.items()})
+        out.update({f"{tag}_w": w, f"{tag}_order": order, f"{tag}_damp": damp,
+                    f"{tag}_q": res[0], f"{tag}_s": res[1], f"{tag}_deq": res[2]})
+        if H is not None:
+            out[f"{tag}_H"] = H
+    save("quip_ldlq.npz", **out)
 
 
 if __name__ == "__main__":

@@ -140,22 +140,21 @@ def test_converter_class_matches_reference_golden(golden, tag, kw):
 
 def test_converter_rejects_unsupported_options():
     with pytest.raises(NotImplementedError):
-        QuIPInt8Converter(actorder=True, use_diagonal_rescaling=False, use_random_permutation=False)
+        QuIPInt8Converter(use_learned_rounding=True)
     with pytest.raises(NotImplementedError):
-        QuIPInt8Converter(**HADAMARD_RTN).convert(torch.zeros(16, 16, device="cuda"), H=torch.eye(16, device="cuda"))
+        QuIPInt8Converter().convert(torch.zeros(16, 16, device="cuda"), activation_scales=torch.ones(16))
 
 
-@pytest.mark.xfail(raises=NotImplementedError, strict=True,
-                   reason="the reference's default converter (act-order, diagonal rescaling, random permutation, "
-                          "LDLQ error feedback) is not implemented")
 @pytest.mark.parametrize("tag", ["np", "p2"])
 def test_converter_reference_defaults_golden(golden, tag):
-    """The reference converter with its default arguments, as it runs in a
-    user's conversion (golden vectors from the reference itself)."""
+    """The reference converter with its default arguments (act-order,
+    diagonal rescaling, random permutation, damping, LDLQ), golden vectors
+    from the reference itself."""
     g = golden("quip_convert_defaults.npz")
     res = QuIPInt8Converter(seed=7).convert(cu(g[f"{tag}_w"]))
     assert np.array_equal(res[0].cpu().numpy(), g[f"{tag}_q"])
     assert np.array_equal(res[1].cpu().numpy(), g[f"{tag}_s"])
+    assert np.array_equal(res[2].cpu().numpy(), g[f"{tag}_deq"])
 
 
 def test_kernel_wrappers_golden(golden):

@@ -94,22 +94,24 @@ def test_workload_definitions():
 
 
 def test_converter_rejects_options_on_cpu():
-    with pytest.raises(NotImplementedError):
-        QuIPInt8Converter(use_random_permutation=True, actorder=False, use_diagonal_rescaling=False)
+    for kw in (dict(use_learned_rounding=True), dict(use_greedy_coordinate_descent=True),
+               dict(use_hadamard=False), dict(ldlq_iterations=2)):
+        with pytest.raises(NotImplementedError):
+            QuIPInt8Converter(**kw)
     with pytest.raises(ValueError):
         QuIPInt8Converter(requant_scheme="axis", **HADAMARD_RTN)
 
 
-def test_converter_keeps_reference_defaults_and_refuses_them():
+def test_converter_keeps_reference_defaults():
     """The reference turns act-order, diagonal rescaling and random
-    permutation on by default (converters/quip_int8.py:33, 50, 52); a drop-in
-    call with default arguments must not silently run another algorithm."""
+    permutation on by default (converters/quip_int8.py:33, 50, 52), and
+    store_transformed turns rescaling off (:83-88)."""
     import inspect
     sig = inspect.signature(QuIPInt8Converter.__init__).parameters
     assert all(sig[k].default is True for k in HADAMARD_RTN)
-    with pytest.raises(NotImplementedError, match="actorder"):
-        QuIPInt8Converter()
-    QuIPInt8Converter(**HADAMARD_RTN)
+    c = QuIPInt8Converter()
+    assert c.actorder and c.use_diagonal_rescaling and c.use_random_permutation and c.percdamp == 0.01
+    assert not QuIPInt8Converter(store_transformed=True).use_diagonal_rescaling
 
 
 def test_conversion_driver_selects_2d_weights_and_names_shards():

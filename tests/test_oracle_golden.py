@@ -203,3 +203,75 @@ def test_gptq_block_golden(golden):
         q, e, w = O.gptq_quant_block(g["w"], g["hinv"], g[f"{tag}_scale"])
         assert np.array_equal(q, g[f"{tag}_q"]) and np.array_equal(e, g[f"{tag}_err"])
         assert np.array_equal(w, g[f"{tag}_w_out"])
+
+
+# ---------------------------------------------------------------- QuIP LDLQ
+LDLQ_CASES = ("id", "wide", "cal", "blk", "st")
+
+
+def ldlq_steps(g, tag):
+    """The oracle's QuIP pass on a fixture case, with the permutations the
+    reference drew (random) and sorted (act-order) taken from the fixture."""
+    import torch
+    w = g[f"{tag}_w"]
+    M, N = w.shape
+    H = g[f"{tag}_H"] if f"{tag}_H" in g else None
+    s_u, s_v, perm = g[f"{tag}_s_u"], g[f"{tag}_s_v"], g[f"{tag}_perm"]
+    D = g[f"{tag}_D"] if g[f"{tag}_D"].size else None
+    if D is not None:
+        wr, hr, D2 = O.diag_rescale(w, H)
+    else:
+        wr, hr, D2 = w, (np.eye(N, dtype=np.float32) if H is None else H), None
+    Np = s_v.shape[0]
+    wrot = O.quip_rotate_weight(wr, s_u, s_v)
+    hpad = np.zeros((Np, Np), np.float32)
+    hpad[:N, :N] = hr
+    hrot = O.quip_rotate_weight(hpad, s_v, s_v)
+    keys = O.damped_order_keys(hrot, perm)
+    order = torch.argsort(torch.from_numpy(keys), descending=True).numpy()  # the reference's own sort
+    wp, hp, damp = O.ldlq_prepare(wrot, hrot, perm, order)
+    return dict(w=w, M=M, N=N, D=D, D2=D2, s_u=s_u, s_v=s_v, perm=perm, order=order, wp=wp, hp=hp, damp=damp,
+                scale=O.quip_ldlq_scale(wp))
+
+
+@pytest.mark.parametrize("tag", LDLQ_CASES)
+def test_ldlq_oracle_pinned(golden, tag):
+    g = golden("quip_ldlq.npz")
+    st = ldlq_steps(g, tag)
+    if st["D"] is not None:
+        assert np.array_equal(st["D2"], st["D"])  # fp64 fourth root of the cascade column sums
+    assert np.array_equal(st["order"], g[f"{tag}_order"])
+    assert st["damp"] == g[f"{tag}_damp"]
+    assert np.array_equal(st["wp"], g[f"{tag}_Wldlq"])
+    assert np.array_equal(st["scale"], g[f"{tag}_scale"])
+    if f"{tag}_Hinv" in g:
+        hinv = O.ldlq_hinv(st["hp"])
+        ref = g[f"{tag}_Hinv"]
+        assert np.abs(hinv - ref).max() <= 1e-9 * np.abs(ref).max()
+        assert (hinv == ref).mean() > 0.999
+    else:
+        hinv = O.ldlq_hinv(st["hp"])
+    q = O.ldlq_pass(st["wp"], hinv, st["scale"], order="blas")
+    assert np.array_equal(q, g[f"{tag}_Qldlq"])
+    q_seq = O.ldlq_pass(st["wp"], hinv, st["scale"], order="seq")
+    assert np.array_equal(q_seq, g[f"{tag}_Qldlq"])
+    qo, deq = O.quip_ldlq_finish(g[f"{tag}_Qldlq"], st["scale"], st["perm"][st["order"]], st["s_u"], st["s_v"],
+                                 st["M"], st["N"], st["D"])
+    if tag == "st":
+        assert np.array_equal(qo, g[f"{tag}_q"])
+    else:
+        assert np.array_equal(deq, g[f"{tag}_deq"])
+        scheme = "block" if tag == "blk" else "tensor"
+        q2, s2 = O.quip_requant(deq, scheme)
+        assert np.array_equal(q2, g[f"{tag}_q"]) and np.array_equal(np.asarray(s2).reshape(-1),
+                                                                    g[f"{tag}_s"].reshape(-1))
+
+
+@pytest.mark.parametrize("shape", [(40, 600), (64, 600), (40, 8), (40, 7), (17, 600), (1, 9), (3000, 40),
+                                   (5000, 5), (257, 1000), (96, 192)])
+def test_col_sumsq_matches_torch_cpu_order(shape):
+    """The cascade / row_sum grouping of torch's CPU sum, bit for bit."""
+    import torch
+    g = torch.Generator().manual_seed(shape[0] * 131 + shape[1])
+    w = torch.randn(*shape, generator=g) * 0.02
+    assert np.array_equal(O.col_sumsq(w.numpy()), (w ** 2).sum(dim=0).numpy())
