@@ -70,11 +70,12 @@ def parse():
     ap.add_argument("--impl", default="qi8", choices=["qi8", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="flux_stack",
-                    choices=["flux_stack", "t5_stack", "dit_mlp", "quip_linear", "conversion"],
+                    choices=["flux_stack", "t5_stack", "dit_mlp", "quip_linear", "conversion", "conversion_ldlq"],
                     help="flux_stack (default): the 228-linear Flux-shaped stack; t5_stack: the 168-linear T5-XXL "
                          "encoder stack (axis-wise scales); dit_mlp: the DiT MLP pair with block-128 K scales; "
                          "quip_linear: one rotated W8A8 linear (K1 rotate -> K2 -> K3); conversion: the 304-tensor "
-                         "QuIP conversion sweep")
+                         "QuIP conversion sweep; conversion_ldlq: one Flux double + single block through the "
+                         "converter with the reference's defaults (rescaling, permutation, act-order, LDLQ)")
     ap.add_argument("--shard", default="auto", choices=["auto", "replica", "columns", "tokens"],
                     help="stacks on N>1 GPUs: tokens (auto) = full weights, each rank 1/N of the tokens; columns = "
                          "every linear column-sharded with its output gathered on every rank; replica = one batch "
@@ -468,6 +469,55 @@ class ConversionCPU:
                 if self.R is not None else "one 3072 x 3072 tensor through the numpy oracle converter, scaled")
 
 
+def ldlq_cost(m: int, n: int) -> float:
+    """Relative cost of the default QuIP conversion of an [m, n] weight:
+    the reference's fp64 chol + cholesky_inverse + chol (4/3 N^3) plus the
+    LDLQ pass (M N^2), at the padded sizes."""
+    mp, np_ = 1 << (m - 1).bit_length(), 1 << (n - 1).bit_length()
+    return 4.0 / 3.0 * np_ ** 3 + mp * np_ ** 2
+
+
+class LdlqCPU:
+    """CPU baseline of the default converter: the reference's
+    QuIPInt8Converter with its defaults (diagonal rescaling, random
+    permutation, act-order, damping, fp64 factorization, LDLQ, per-row
+    requant) on one 3072 x 3072 tensor, scaled to the 10-tensor block set by
+    :func:`ldlq_cost`.  (At N_pad >= 8192 the reference's CPU-only run takes
+    its checkpointed LDLQ branch, so the larger tensors are not sampled.)"""
+
+    def __init__(self):
+        from convert_to_quant_quip_int8_b200.workloads import ldlq_block_tensors
+        self.R = reference_package()
+        self.kind = "reference" if self.R is not None else "port"
+        self.w = (torch.randn(3072, 3072, generator=_gen(0)) * 0.02).to(torch.bfloat16)
+        shapes = [(m, n) for _, m, n in ldlq_block_tensors()]
+        self.scale = sum(ldlq_cost(m, n) for m, n in shapes) / ldlq_cost(3072, 3072)
+        self.n_tensors = len(shapes)
+
+    def step(self):
+        if self.R is not None:
+            return self.R["QuIPInt8Converter"](device="cpu", seed=1000).convert(self.w.clone())
+        import oracle as O
+        from convert_to_quant_quip_int8_b200.workloads import quip_signs
+        w = self.w.float().numpy()
+        wr, hr, D = O.diag_rescale(w, None)
+        su, sv = (t.numpy() for t in quip_signs(1000, 4096, 4096))
+        wrot = O.quip_rotate_weight(wr, su, sv)
+        hpad = np.zeros((4096, 4096), np.float32)
+        hpad[:3072, :3072] = hr
+        hrot = O.quip_rotate_weight(hpad, sv, sv)
+        perm = np.random.default_rng(1000).permutation(4096)
+        order = np.argsort(-O.damped_order_keys(hrot, perm), kind="stable")
+        wp, hp, _ = O.ldlq_prepare(wrot, hrot, perm, order)
+        q = O.ldlq_pass(wp, O.ldlq_hinv(hp), O.quip_ldlq_scale(wp))
+        return q
+
+    def sample(self):
+        return ("one 3072 x 3072 tensor through the reference's QuIPInt8Converter with its defaults, scaled to "
+                "the 10-tensor block set by 4/3 N^3 + M N^2 at the padded sizes" if self.R is not None else
+                "one 3072 x 3072 tensor through the numpy oracle's default-converter steps, scaled")
+
+
 def cpu_timed(step, steps, warmup):
     for _ in range(max(0, warmup)):
         step()
@@ -491,7 +541,7 @@ def cpu_point(workload: str, steps: int = 1, warmup: int = 1):
         c = QuipLinearCPU()
         med = cpu_timed(c.step, steps, warmup)
         return c.ops / med / 1e12, "TOPS", med, threads, c.kind, c.sample()
-    c = ConversionCPU()
+    c = LdlqCPU() if workload == "conversion_ldlq" else ConversionCPU()
     med = cpu_timed(c.step, steps, warmup)
     return c.n_tensors / (med * c.scale), "tensors/s", med * c.scale, threads, c.kind, c.sample()
 
@@ -991,6 +1041,133 @@ def main_conversion(args):
     finish(world)
 
 
+LDLQ_METRIC = "QuIP default-converter tensors/s (one Flux double + single block, 10 tensors, 0.34 B params)"
+FP64_NOMINAL_TFLOPS = 37.0  # B200 dense fp64 (vector and tensor), nominal
+
+
+def ldlq_launches(m: int, n: int) -> int:
+    """libqi8 kernel launches of one default conversion (diagonal rescaling,
+    per-row requant) of an [m, n] weight."""
+    mp, np_ = 1 << (m - 1).bit_length(), 1 << (n - 1).bit_length()
+    colp = lambda rows: 1 if rows <= 512 else 2  # column FWHT passes
+    leaves = max(1, np_ // 64)  # recursive Cholesky-inverse: 64-wide leaves, 4 GEMMs per inner node
+    hinv = leaves + 4 * (leaves - 1) + 1
+    nbk = (np_ + 127) // 128
+    return (1 + 2 + (colp(mp) + 1) + (colp(np_) + 1) + 2 + hinv + (2 * nbk - 1) + 1 + (1 + colp(mp)) + 1 + 1)
+
+
+def main_conversion_ldlq(args):
+    """The converter with the reference's defaults (QuIPInt8Converter(seed),
+    converters/quip_int8.py:1031-1669) on the 10 weights of one Flux double
+    and one single block, bf16 resident in HBM; one step converts all ten
+    (per-row tensorwise requant).  Tensors are partitioned over ranks like
+    the conversion sweep (no collective)."""
+    from convert_to_quant_quip_int8_b200 import ops, sharding
+    from convert_to_quant_quip_int8_b200.converters.quip_int8 import QuIPInt8Converter
+    from convert_to_quant_quip_int8_b200.workloads import ldlq_block_tensors
+
+    rank, world, local = dist_init()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    shapes = [(m, n) for _, m, n in ldlq_block_tensors()]
+    mine = sharding.plan_partition(shapes, world)[rank]
+    gen = torch.Generator(device=device)
+    weights = []
+    for i in mine:
+        gen.manual_seed(70 + i)
+        weights.append((torch.randn(*shapes[i], generator=gen, device=device) * 0.02).to(torch.bfloat16))
+    conv = QuIPInt8Converter(seed=1000, device=str(device))
+
+    def step():
+        for w in weights:
+            conv.convert(w)
+
+    step()
+    torch.cuda.synchronize(device)
+    steps = max(1, min(args.steps, 3))
+    ms, clocks = timed_region(step, steps, world, device)
+    ops.device_status()
+    value = len(shapes) * steps / (ms / 1e3)
+    params = sum(m * n for m, n in shapes)
+
+    # the dominant kernels (the fp64 factorization) timed live with CUDA events on one more step
+    hinv_times = {}
+    orig = ops.hinv_upper
+
+    def timed_hinv(h_rev):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = orig(h_rev)
+        b.record()
+        hinv_times.setdefault(h_rev.shape[0], []).append((a, b))
+        return out
+
+    ops.hinv_upper = timed_hinv
+    try:
+        step()
+    finally:
+        ops.hinv_upper = orig
+    torch.cuda.synchronize(device)
+    step_ms = ms / steps
+    fact_ms = sum(a.elapsed_time(b) for v in hinv_times.values() for a, b in v)
+    nbig = max(hinv_times) if hinv_times else 0
+    big = [a.elapsed_time(b) for a, b in hinv_times.get(nbig, [])]
+
+    # e2e: pinned host bf16 -> device -> converter -> pinned host int8 + scales
+    host_w = [w.cpu().pin_memory() for w in weights]
+    host_q = [(torch.empty(w.shape, dtype=torch.int8).pin_memory(),
+               torch.empty((w.shape[0], 1), dtype=torch.float32).pin_memory()) for w in weights]
+    h2d = d2h = 0
+
+    def e2e_step():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        for hw, (hq, hs) in zip(host_w, host_q):
+            w = hw.to(device, non_blocking=True)
+            q, s = conv.convert(w)[:2]
+            hq.copy_(q, non_blocking=True)
+            hs.copy_(s.reshape(hs.shape), non_blocking=True)
+            h2d += hw.numel() * 2
+            d2h += hq.numel() + hs.numel() * 4
+
+    e2e_step()
+    barrier(world)
+    e2e_ms = max_over_ranks(event_time(e2e_step, 1, device), world, device)
+    if rank != 0:
+        finish(world)
+        return
+    achieved = (2.0 / 3.0) * nbig ** 3 / (statistics.mean(big) / 1e3) / 1e12 if big else None
+    line = {
+        "metric": LDLQ_METRIC, "value": round(value, 3), "unit": "tensors/s", "n_gpus": world, "steps": steps,
+        "warmup": 1, "ms_per_step": round(step_ms, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp64 factorization, fp32 LDLQ, int8 out",
+        "weight_gb_per_s": round(params * 2 / (step_ms / 1e3) / 1e9, 2),
+        "data": "synthetic (seeded N(0,0.02) bf16 weights resident in HBM)",
+        "config": {"workload": "QuIPInt8Converter defaults (diagonal rescaling, random permutation, act-order, "
+                               "damping, fp64 Hessian factorization, blocked LDLQ, per-row requant), H = identity, "
+                               "Flux double block (img + txt: qkv, proj, mlp0, mlp2) + single block "
+                               "(linear1, linear2)", "params": params,
+                   "parallelism": f"tensor-partitioned x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": round(len(shapes) / (e2e_ms / 1e3), 3), "unit": "tensors/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 2),
+                "path": "pinned host bf16 -> device -> QuIPInt8Converter.convert -> pinned host int8 + scales"},
+        "roofline": {"bound": "fp64", "achieved": round(achieved, 2) if achieved else None,
+                     "peak": FP64_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+                     "frac": round(achieved / FP64_NOMINAL_TFLOPS, 4) if achieved else None, "traffic": None,
+                     "algorithmic": f"2/3 N^3 fp64 flops per factorization (Cholesky N^3/3 + triangular inverse "
+                                    f"N^3/3), N = {nbig}",
+                     "kernel": "qi8_hinv_upper (potf2_inv_kernel + dgemm_kernel launches)",
+                     "share_of_step": round(fact_ms / step_ms, 3),
+                     "peak_note": "nominal B200 fp64 (no measured fp64 peak on this pool)"},
+        "gpu_launches": steps * sum(ldlq_launches(*shapes[i]) for i in mine), "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        v, unit, sec, threads, kind, sample = cpu_point("conversion_ldlq")
+        line["cpu_baseline"] = cpu_baseline_field(v, unit, threads, kind, sample, sec)
+    print(json.dumps(line), flush=True)
+    finish(world)
+
+
 # ======================================================= reference arm
 def main_reference(args):
     """The reference's CPU path on this box's host cores (rank 0 only), on
@@ -1027,9 +1204,10 @@ def main_reference(args):
         value, unit, sec, threads, kind, sample = cpu_point(wl, steps=steps, warmup=min(args.warmup, 1))
         metric = {"dit_mlp": "W8A8 QuIP linear TOPS (DiT MLP pair, block-128 K scales)",
                   "quip_linear": "QuIP W8A8 rotated linear TOPS (transformed storage, tensorwise scale)",
-                  "conversion": "QuIP conversion sweep tensors/s (304 tensors, 12.9 B params)"}[wl]
+                  "conversion": "QuIP conversion sweep tensors/s (304 tensors, 12.9 B params)",
+                  "conversion_ldlq": LDLQ_METRIC}[wl]
         config = {"workload": wl, "parallelism": "cpu"}
-        scaling = "strong" if wl == "conversion" else "weak"
+        scaling = "strong" if wl.startswith("conversion") else "weak"
         ms_step = sec * 1e3
     line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 2),
@@ -1051,6 +1229,8 @@ def main():
         return main_dit_mlp(args)
     if args.workload == "quip_linear":
         return main_quip_linear(args)
+    if args.workload == "conversion_ldlq":
+        return main_conversion_ldlq(args)
     return main_conversion(args)
 
 

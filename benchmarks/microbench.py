@@ -5,6 +5,7 @@
     python benchmarks/microbench.py gemm     # K2 block-scaled / per-row GEMM
     python benchmarks/microbench.py gemm_stack  # K2 on the Flux / T5 stacks' largest linears
     python benchmarks/microbench.py convert  # K4 QuIP conversion
+    python benchmarks/microbench.py ldlq     # default converter: fp64 Hinv factorization, LDLQ pass
 
 Each case is timed with CUDA events around one launch, median of ``--iters``
 launches, with a 256 MB buffer rewritten between launches so every launch
@@ -154,9 +155,51 @@ def convert_cases(run, dev):
     return res
 
 
+LDLQ_SIZES = (4096, 16384)
+
+
+def ldlq_cases(run, dev):
+    """qi8_hinv_upper (fp64: Cholesky N^3/3 + triangular inverse N^3/3 flops;
+    each launch restores its input first, an N^2 fp64 copy) and qi8_ldlq
+    (fp32: M N^2 flops, the input copied back first)."""
+    res = {}
+    for N in LDLQ_SIZES:
+        g = torch.Generator(device=dev).manual_seed(N)
+        x = torch.randn(N, N, device=dev, dtype=torch.float64, generator=g)
+        h = x @ x.t() / N + torch.eye(N, device=dev, dtype=torch.float64)
+        del x
+        hrev = torch.tril(h.flip(0).flip(1)).contiguous()
+        del h
+        h2 = torch.empty_like(hrev)
+        holder = {}
+
+        def fact():
+            h2.copy_(hrev)
+            holder["hinv"] = ops.hinv_upper(h2)[0]
+        us = run(fact)
+        res[f"hinv_upper_{N}"] = [us, (2.0 / 3.0) * N ** 3 / us / 1e6]
+        if "hinv" not in holder:
+            fact()
+        hinv = holder.pop("hinv")
+        del hrev, h2
+        M = 4096
+        w0 = torch.randn(M, N, device=dev, generator=g) * 0.02
+        sc = (w0.abs().amax(1, keepdim=True) / 127).clamp(min=1e-12)
+        w = torch.empty_like(w0)
+
+        def pass_():
+            w.copy_(w0)
+            ops.ldlq(w, hinv, sc)
+        us = run(pass_)
+        res[f"ldlq_{M}x{N}"] = [us, M * N * N / us / 1e6]
+        del w0, w, hinv
+        torch.cuda.empty_cache()
+    return res
+
+
 CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "gemm_stack": gemm_stack_cases,
          "gemm_tile": gemm_tile_cases,
-         "convert": convert_cases}
+         "convert": convert_cases, "ldlq": ldlq_cases}
 
 
 def main(argv=None):
@@ -164,7 +207,11 @@ def main(argv=None):
     ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--profile", action="store_true")
+    ap.add_argument("--small", action="store_true", help="ldlq: only the 4096 size (the form for ncu captures)")
     args = ap.parse_args(argv)
+    if args.small:
+        global LDLQ_SIZES
+        LDLQ_SIZES = (4096,)
     dev = torch.device("cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     res = CASES[args.case](_timer(flush, args.iters, args.profile), dev)

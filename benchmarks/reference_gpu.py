@@ -17,7 +17,12 @@ come from HBM):
 * ``triton_hadamard_transform`` + ``quantize_int8_axiswise`` (the reference's
   rotated-activation steps, comfy/int8_kernels.py:1424-1428 and
   comfy/quant_ops.py:469) vs K1 ``qi8_rotate_quant_rows``;
-* ``act_quant`` (comfy/int8_kernels.py:96) vs ``qi8_quant_rows`` block mode.
+* ``act_quant`` (comfy/int8_kernels.py:96) vs ``qi8_quant_rows`` block mode;
+* ``QuIPInt8Converter(device="cuda", seed)`` with its defaults
+  (converters/quip_int8.py:1031-1669: rescaling, permutation, act-order,
+  LDLQ; its own device placement and bf16 autocast) vs this package's
+  converter, wall clock per tensor (1 warm-up, median of 3), with the
+  fraction of int8 codes the two agree on.
 
 Prints one JSON object: case -> {"ref_us", "qi8_us", "cublas_us"?, "speedup"}.
 
@@ -135,6 +140,30 @@ def main():
         ours = run(lambda: ops.rotate_quant_rows(xr, sv, n))
         bytes_ = T * n * 3 + T * 4
         put(f"rotate_quant_{T}x{n}", run(ref_rot), ours, qi8_gbs=bytes_ / ours / 1e3)
+    # the default QuIP converter, whole tensor (host syncs inside both)
+    import time
+    from convert_to_quant.converters.quip_int8 import QuIPInt8Converter as RefConv
+    from convert_to_quant_quip_int8_b200.converters.quip_int8 import QuIPInt8Converter as Conv
+
+    def wall(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            out = fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        return sorted(ts)[1] * 1e6, out
+
+    for M, N in [(3072, 3072), (12288, 3072), (3072, 12288)]:
+        w = (torch.randn(M, N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        logging.disable(logging.WARNING)
+        ref_us, ref_out = wall(lambda: RefConv(device="cuda", seed=1).convert(w.clone()))
+        logging.disable(logging.NOTSET)
+        our_us, our_out = wall(lambda: Conv(seed=1).convert(w))
+        agree = (ref_out[0].to(dev) == our_out[0]).float().mean().item()
+        put(f"quip_convert_defaults_{M}x{N}", ref_us, our_us, q_agreement=agree * 100)
     print(json.dumps(res), flush=True)
 
 

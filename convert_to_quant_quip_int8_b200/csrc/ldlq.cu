@@ -16,10 +16,9 @@
 // Hessian factorization.  The reference computes chol(H) -> cholesky_inverse
 // -> chol(., upper=True) in fp64.  U (H^-1 = U^T U, U upper, positive
 // diagonal) is unique, and with J the index reversal U = J L2^-1 J where
-// L2 = chol(J H J): one blocked Cholesky (64-wide diagonal blocks, fp64 SIMT
-// GEMM updates) and one triangular inverse (recursive 2x2 block doubling
-// over the 64-wide inverses the Cholesky leaves on its diagonal), about a
-// third of the reference's flops.  The factorization reads the lower
+// L2 = chol(J H J): a recursive Cholesky that carries the inverse along
+// (halves split until 64-wide leaves, every off-diagonal step an h x h x h
+// fp64 SIMT GEMM), 2/3 N^3 flops, half of the reference's.  The factorization reads the lower
 // triangle of the damped Hessian, as LAPACK's potrf does in the reference;
 // the rotated Hessian is not bit-symmetric (the two 1-D transforms of each
 // entry pair round in different orders).
@@ -295,8 +294,17 @@ __global__ void __launch_bounds__(256) potf2_inv_kernel(double* A, int64_t ld, i
 // operands restrict the k range per tile: triA (A lower) k < m0 + 64;
 // triB (B lower as stored) k >= n0 without transB, k < n0 + 64 with it.
 // lowerC skips tiles strictly above the diagonal.  M, N multiples of 64,
-// the k range a multiple of 16.  A and C may alias when one tile column
-// covers N (each CTA reads its rows of A before it writes C).
+// the k range a multiple of 16; every offset fits in 32 bits (N <= 32768).
+// C must not alias A or B.
+//
+// 256 threads, 4x4 outputs per thread (rows 2ty, 2ty+1, 32+2ty, 33+2ty and
+// the same pattern of columns in tx), 16-deep k chunks: the next chunk is
+// loaded into registers while the current one is multiplied out of shared
+// memory (two buffers, one barrier per chunk).  Shared tiles are k-major
+// [k][64] with element (k, j) at column j ^ k, so the coalesced global
+// loads (16 consecutive k per row) store without bank conflicts and each
+// thread's aligned pairs stay pairs (read as one 16-byte load, swapped back
+// in registers when k is odd).
 struct DGemm {
   const double* A;
   const double* B;
@@ -306,65 +314,89 @@ struct DGemm {
   double alpha;
 };
 
-__global__ void __launch_bounds__(256) dgemm_kernel(DGemm g) {
-  const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+__global__ void __launch_bounds__(256, 2) dgemm_kernel(DGemm g) {
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   if (g.lowerC && m0 + 64 <= n0) return;
-  const double* A = g.A + (int64_t)blockIdx.z * g.sA;
-  const double* B = g.B + (int64_t)blockIdx.z * g.sB;
+  const double* __restrict__ A = g.A + (int64_t)blockIdx.z * g.sA;
+  const double* __restrict__ B = g.B + (int64_t)blockIdx.z * g.sB;
   double* C = g.C + (int64_t)blockIdx.z * g.sC;
-  int64_t k0 = 0, k1 = g.K;
+  const int lda = (int)g.lda, ldb = (int)g.ldb, ldc = (int)g.ldc;
+  int k0 = 0, k1 = g.K;
   if (g.triA) k1 = min(k1, m0 + 64);
   if (g.triB) {
     if (g.transB) k1 = min(k1, n0 + 64);
     else k0 = n0;
   }
-  __shared__ __align__(16) double As[16][66];
-  __shared__ __align__(16) double Bs[16][66];
+  __shared__ __align__(16) double As[2][16][64];
+  __shared__ __align__(16) double Bs[2][16][64];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  // load slots: A rows (tid >> 4) + 16 r, k = tid & 15; B likewise (transB) or k = tid >> 6 + 4 r, n = tid & 63
+  const int lk = tid & 15, lm = tid >> 4;
+  const int bk = tid >> 6, bn = tid & 63;
+  double ra[4], rb[4];
+  auto gload = [&](int kb) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) ra[r] = A[(m0 + lm + 16 * r) * lda + kb + lk];
+    if (g.transB) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) rb[r] = B[(n0 + lm + 16 * r) * ldb + kb + lk];
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) rb[r] = B[(kb + bk + 4 * r) * ldb + n0 + bn];
+    }
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) As[buf][lk][(lm + 16 * r) ^ lk] = ra[r];
+    if (g.transB) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) Bs[buf][lk][(lm + 16 * r) ^ lk] = rb[r];
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) Bs[buf][bk + 4 * r][bn ^ (bk + 4 * r)] = rb[r];
+    }
+  };
   double acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-  for (int64_t kb = k0; kb < k1; kb += 16) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int e = tid + 256 * r, m = e >> 4, k = e & 15;
-      As[k][m] = A[(m0 + m) * g.lda + kb + k];
-    }
-    if (g.transB) {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = tid + 256 * r, n = e >> 4, k = e & 15;
-        Bs[k][n] = B[(n0 + n) * g.ldb + kb + k];
-      }
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int e = tid + 256 * r, k = e >> 6, n = e & 63;
-        Bs[k][n] = B[(kb + k) * g.ldb + n0 + n];
-      }
-    }
-    __syncthreads();
+  if (k0 < k1) {
+    gload(k0);
+    sstore(0);
+  }
+  __syncthreads();
+  int buf = 0;
+  for (int kb = k0; kb < k1; kb += 16) {
+    const bool more = kb + 16 < k1;
+    if (more) gload(kb + 16);
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      const double2 a01 = *reinterpret_cast<const double2*>(&As[k][ty * 4]);
-      const double2 a23 = *reinterpret_cast<const double2*>(&As[k][ty * 4 + 2]);
-      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[k][tx * 4]);
-      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[k][tx * 4 + 2]);
-      const double av[4] = {a01.x, a01.y, a23.x, a23.y}, bv[4] = {b01.x, b01.y, b23.x, b23.y};
+      const int pa = (ty * 2) ^ (k & 14), pb = (tx * 2) ^ (k & 14);
+      const double2 a01 = *reinterpret_cast<const double2*>(&As[buf][k][pa]);
+      const double2 a23 = *reinterpret_cast<const double2*>(&As[buf][k][pa + 32]);
+      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[buf][k][pb]);
+      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[buf][k][pb + 32]);
+      const bool sw = k & 1;
+      const double av[4] = {sw ? a01.y : a01.x, sw ? a01.x : a01.y, sw ? a23.y : a23.x, sw ? a23.x : a23.y};
+      const double bv[4] = {sw ? b01.y : b01.x, sw ? b01.x : b01.y, sw ? b23.y : b23.x, sw ? b23.x : b23.y};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
     }
+    if (more) sstore(buf ^ 1);
     __syncthreads();
+    buf ^= 1;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    double* c = C + (m0 + ty * 4 + i) * g.ldc + n0 + tx * 4;
+    double* c = C + (m0 + (i < 2 ? 0 : 32) + ty * 2 + (i & 1)) * ldc + n0 + tx * 2;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) c[j] = g.accumulate ? fma(g.alpha, acc[i][j], c[j]) : g.alpha * acc[i][j];
+    for (int j = 0; j < 4; ++j) {
+      double* cj = c + (j < 2 ? 0 : 32) + (j & 1);
+      *cj = g.accumulate ? fma(g.alpha, acc[i][j], *cj) : g.alpha * acc[i][j];
+    }
   }
 }
 
@@ -593,9 +625,62 @@ extern "C" int qi8_ldlq_prepare(const float* w_rot, const float* h_rot, int64_t 
   return check_cuda(cudaGetLastError(), "ldlq_gather_h_kernel launch");
 }
 
+namespace {
+// Recursive Cholesky with the inverse carried along: for the n x n diagonal
+// block at A + off (N + 1) (lower triangle on entry), on exit the block holds
+// X = chol(block)^-1 (lower, zeros above).  With h = n / 2:
+//   X11 = chol_inv(A11); L21 = A21 X11^T (into t1[level]); A22 -= L21 L21^T;
+//   X22 = chol_inv(A22); X21 = -(X22 L21) X11 (through t3).
+// Every GEMM is h x h x h with the triangular operand's zero tiles skipped;
+// the 64-wide leaves are factored and inverted by potf2_inv_kernel.
+struct HinvCtx {
+  double* A;
+  int64_t N;
+  double* t1[16];
+  double* t3;
+  int* info;
+  cudaStream_t st;
+};
+
+int chol_inv(const HinvCtx& c, int64_t off, int64_t n, int level) {
+  const int64_t N = c.N;
+  double* A11 = c.A + off * (N + 1);
+  if (n <= PB) {
+    potf2_inv_kernel<<<1, 256, sizeof(double) * PB * (PB + 1), c.st>>>(A11, N, (int)n, off, c.info);
+    return check_cuda(cudaGetLastError(), "potf2_inv_kernel launch");
+  }
+  const int64_t h = n / 2;
+  double* A21 = A11 + h * N;
+  double* A22 = A11 + h * (N + 1);
+  double* T1 = c.t1[level];
+  int rc = chol_inv(c, off, h, level + 1);
+  if (rc != QI8_OK) return rc;
+  DGemm a{};  // L21 = A21 @ X11^T
+  a.A = A21; a.lda = N; a.B = A11; a.ldb = N; a.transB = 1; a.triB = 1;
+  a.C = T1; a.ldc = h; a.M = a.N = a.K = (int)h; a.alpha = 1.0;
+  if ((rc = dgemm(a, 1, c.st)) != QI8_OK) return rc;
+  DGemm b{};  // A22 -= L21 @ L21^T (lower tiles)
+  b.A = T1; b.lda = h; b.B = T1; b.ldb = h; b.transB = 1; b.lowerC = 1; b.accumulate = 1;
+  b.C = A22; b.ldc = N; b.M = b.N = b.K = (int)h; b.alpha = -1.0;
+  if ((rc = dgemm(b, 1, c.st)) != QI8_OK) return rc;
+  if ((rc = chol_inv(c, off + h, h, level + 1)) != QI8_OK) return rc;
+  DGemm d{};  // T3 = X22 @ L21
+  d.A = A22; d.lda = N; d.triA = 1; d.B = T1; d.ldb = h;
+  d.C = c.t3; d.ldc = h; d.M = d.N = d.K = (int)h; d.alpha = 1.0;
+  if ((rc = dgemm(d, 1, c.st)) != QI8_OK) return rc;
+  DGemm e{};  // X21 = -(T3 @ X11)
+  e.A = c.t3; e.lda = h; e.B = A11; e.ldb = N; e.triB = 1;
+  e.C = A21; e.ldc = N; e.M = e.N = e.K = (int)h; e.alpha = -1.0;
+  return dgemm(e, 1, c.st);
+}
+}  // namespace
+
 extern "C" int64_t qi8_hinv_workspace_bytes(int64_t N) {
   if (N < 1) return -1;
-  return (N >= 2 * PB ? (N * N / 4) * (int64_t)sizeof(double) : 0) + 256;
+  int64_t elems = 0;
+  for (int64_t h = N / 2; h >= PB; h /= 2) elems += h * h;  // t1 per level
+  elems += (N / 2 >= PB) ? (N / 2) * (N / 2) : 0;             // t3
+  return elems * (int64_t)sizeof(double) + 256 * 16;
 }
 
 extern "C" int qi8_hinv_upper(double* h_rev, int64_t N, float* hinv_out, int* info, void* workspace,
@@ -608,44 +693,21 @@ extern "C" int qi8_hinv_upper(double* h_rev, int64_t N, float* hinv_out, int* in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = check_cuda(cudaMemsetAsync(info, 0, sizeof(int), st), "cudaMemsetAsync");
   if (rc != QI8_OK) return rc;
-  const int nb = (int)(N < PB ? N : PB);
-  const size_t psmem = sizeof(double) * PB * (PB + 1);
-  rc = set_smem((const void*)potf2_inv_kernel, psmem);
+  rc = set_smem((const void*)potf2_inv_kernel, sizeof(double) * PB * (PB + 1));
   if (rc != QI8_OK) return rc;
-  // blocked right-looking Cholesky of J H J; diagonal blocks replaced by their inverses
-  for (int64_t k0 = 0; k0 < N; k0 += nb) {
-    double* akk = h_rev + k0 * N + k0;
-    potf2_inv_kernel<<<1, 256, psmem, st>>>(akk, N, nb, k0, info);
-    if ((rc = check_cuda(cudaGetLastError(), "potf2_inv_kernel launch")) != QI8_OK) return rc;
-    const int64_t R = N - k0 - nb;
-    if (R == 0) break;
-    double* panel = h_rev + (k0 + nb) * N + k0;
-    DGemm t{};  // panel := panel @ inv(L_kk)^T
-    t.A = panel; t.lda = N; t.B = akk; t.ldb = N; t.C = panel; t.ldc = N;
-    t.M = (int)R; t.N = nb; t.K = nb; t.transB = 1; t.triB = 1; t.alpha = 1.0;
-    if ((rc = dgemm(t, 1, st)) != QI8_OK) return rc;
-    DGemm u{};  // trailing lower triangle -= panel @ panel^T
-    u.A = panel; u.lda = N; u.B = panel; u.ldb = N; u.C = h_rev + (k0 + nb) * (N + 1); u.ldc = N;
-    u.M = (int)R; u.N = (int)R; u.K = nb; u.transB = 1; u.lowerC = 1; u.accumulate = 1; u.alpha = -1.0;
-    if ((rc = dgemm(u, 1, st)) != QI8_OK) return rc;
+  HinvCtx c{};
+  c.A = h_rev;
+  c.N = N;
+  c.info = info;
+  c.st = st;
+  char* p = static_cast<char*>(workspace);
+  int level = 0;
+  for (int64_t h = N / 2; h >= PB; h /= 2, ++level) {
+    c.t1[level] = reinterpret_cast<double*>(p);
+    p += ((h * h * (int64_t)sizeof(double) + 255) / 256) * 256;
   }
-  // triangular inverse by block doubling: inv([[A, 0], [B, C]]) = [[Ai, 0], [-Ci B Ai, Ci]]
-  double* T = static_cast<double*>(workspace);
-  for (int64_t s = nb; s < N; s *= 2) {
-    const int pairs = (int)(N / (2 * s));
-    DGemm a{};  // T_p = B_p @ Ai_p (Ai lower)
-    a.A = h_rev + s * N; a.lda = N; a.sA = 2 * s * (N + 1);
-    a.B = h_rev; a.ldb = N; a.sB = 2 * s * (N + 1); a.triB = 1;
-    a.C = T; a.ldc = s; a.sC = s * s;
-    a.M = a.N = a.K = (int)s; a.alpha = 1.0;
-    if ((rc = dgemm(a, pairs, st)) != QI8_OK) return rc;
-    DGemm b{};  // B_p := -(Ci_p @ T_p) (Ci lower)
-    b.A = h_rev + s * (N + 1); b.lda = N; b.sA = 2 * s * (N + 1); b.triA = 1;
-    b.B = T; b.ldb = s; b.sB = s * s;
-    b.C = h_rev + s * N; b.ldc = N; b.sC = 2 * s * (N + 1);
-    b.M = b.N = b.K = (int)s; b.alpha = -1.0;
-    if ((rc = dgemm(b, pairs, st)) != QI8_OK) return rc;
-  }
+  c.t3 = reinterpret_cast<double*>(p);
+  if ((rc = chol_inv(c, 0, N, 0)) != QI8_OK) return rc;
   hinv_out_kernel<<<grid_for(N * N, 256), 256, 0, st>>>(h_rev, N, hinv_out);
   return check_cuda(cudaGetLastError(), "hinv_out_kernel launch");
 }

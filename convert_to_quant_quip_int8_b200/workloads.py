@@ -127,6 +127,13 @@ def conversion_sweep_tensors() -> List[Tuple[str, int, int]]:
 
 
 # ---------------------------------------------------- T5-XXL encoder stack
+def ldlq_block_tensors() -> List[Tuple[str, int, int]]:
+    """The weights of one Flux double-stream block (img and txt: qkv, proj,
+    mlp0, mlp2) and one single-stream block (linear1, linear2): 10 tensors,
+    ``(name, out, in)``, for the converter with the reference's defaults."""
+    return [t for t in conversion_sweep_tensors() if t[0].startswith(("double0.", "single0.0."))]
+
+
 def t5_linears() -> List[Tuple[str, int, int, int]]:
     """(name, tokens, in_features, out_features) of the 168 linears of a
     T5-XXL-shaped encoder forward (d_model 4096, d_ff 10240, 24 layers,
