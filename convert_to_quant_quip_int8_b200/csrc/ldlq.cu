@@ -18,7 +18,7 @@
 // diagonal) is unique, and with J the index reversal U = J L2^-1 J where
 // L2 = chol(J H J): a recursive Cholesky that carries the inverse along
 // (halves split until 64-wide leaves, every off-diagonal step an h x h x h
-// fp64 SIMT GEMM), 2/3 N^3 flops, half of the reference's.  The factorization reads the lower
+// fp64 GEMM on the tensor cores), 2/3 N^3 flops, half of the reference's.  The factorization reads the lower
 // triangle of the damped Hessian, as LAPACK's potrf does in the reference;
 // the rotated Hessian is not bit-symmetric (the two 1-D transforms of each
 // entry pair round in different orders).
@@ -241,10 +241,20 @@ __global__ void eye_kernel(int64_t N, float* __restrict__ out) {
 // ld), then its inverse, written back over the block (zeros above the
 // diagonal).  A non-positive or non-finite pivot records its global index + 1
 // in *info (first failure wins) and continues with pivot 1.
+//
+// Factorization: one barrier per column.  At step j every thread reads the
+// (final) column j of the working matrix a, takes the pivot d = sqrt(a_jj)
+// itself, writes its entries of L[:, j] = a[:, j] * (1 / d) into l (a separate
+// array, so no thread overwrites what another still reads) and applies its
+// share of the rank-1 update to the trailing lower triangle of a.  Inverse:
+// one warp per column c solves L x = e_c right-looking with the diagonal
+// reciprocals precomputed; lane holds rows lane and lane + 32.
 constexpr int PB = 64;
 __global__ void __launch_bounds__(256) potf2_inv_kernel(double* A, int64_t ld, int nb, int64_t base, int* info) {
   extern __shared__ double psm[];
   double (*a)[PB + 1] = reinterpret_cast<double (*)[PB + 1]>(psm);
+  double (*l)[PB + 1] = reinterpret_cast<double (*)[PB + 1]>(psm + PB * (PB + 1));
+  double* rd = psm + 2 * PB * (PB + 1);  // reciprocals of L's diagonal
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int e = tid; e < nb * nb; e += 256) {
     const int i = e / nb, j = e % nb;
@@ -252,37 +262,36 @@ __global__ void __launch_bounds__(256) potf2_inv_kernel(double* A, int64_t ld, i
   }
   __syncthreads();
   for (int j = 0; j < nb; ++j) {
-    if (tid == 0) {
-      double d = a[j][j];
-      if (!(d > 0.0) || !isfinite(d)) {
-        atomicCAS(info, 0, (int)(base + j + 1));
-        d = 1.0;
+    double d = a[j][j];
+    const bool bad = !(d > 0.0) || !isfinite(d);
+    if (bad) d = 1.0;
+    if (bad && tid == 0) atomicCAS(info, 0, (int)(base + j + 1));
+    d = sqrt(d);
+    const double r = 1.0 / d;
+    const int m = nb - j;  // rows j..nb-1 of column j
+    for (int i = tid; i < m; i += 256) l[j + i][j] = i == 0 ? d : a[j + i][j] * r;
+    const int t = m - 1;   // trailing rows / columns j+1..nb-1
+    for (int e = tid; e < t * t; e += 256) {
+      const int ii = e / t, ll = e % t;
+      if (ll <= ii) {
+        const double li = a[j + 1 + ii][j] * r, lj = a[j + 1 + ll][j] * r;
+        a[j + 1 + ii][j + 1 + ll] = fma(-li, lj, a[j + 1 + ii][j + 1 + ll]);
       }
-      a[j][j] = sqrt(d);
-    }
-    __syncthreads();
-    const double djj = a[j][j];
-    for (int i = j + 1 + tid; i < nb; i += 256) a[i][j] = a[i][j] / djj;
-    __syncthreads();
-    const int m = nb - j - 1;
-    for (int e = tid; e < m * m; e += 256) {
-      const int ii = e / m, ll = e % m;
-      if (ll <= ii) a[j + 1 + ii][j + 1 + ll] = fma(-a[j + 1 + ii][j], a[j + 1 + ll][j], a[j + 1 + ii][j + 1 + ll]);
     }
     __syncthreads();
   }
-  // inverse, one warp per column c: solve L x = e_c right-looking; lane holds
-  // rows lane and lane + 32
+  for (int i = tid; i < nb; i += 256) rd[i] = 1.0 / l[i][i];
+  __syncthreads();
   const unsigned full = 0xffffffffu;
   for (int c = warp; c < nb; c += 8) {
     double x0 = lane == c ? 1.0 : 0.0, x1 = lane + 32 == c ? 1.0 : 0.0;
     for (int t = c; t < nb; ++t) {
       double xt = t < 32 ? __shfl_sync(full, x0, t) : __shfl_sync(full, x1, t - 32);
-      xt = xt / a[t][t];
+      xt *= rd[t];
       if (lane == t) x0 = xt;
       if (lane + 32 == t) x1 = xt;
-      if (lane > t && lane < nb) x0 = fma(-a[lane][t], xt, x0);
-      if (lane + 32 > t && lane + 32 < nb) x1 = fma(-a[lane + 32][t], xt, x1);
+      if (lane > t && lane < nb) x0 = fma(-l[lane][t], xt, x0);
+      if (lane + 32 > t && lane + 32 < nb) x1 = fma(-l[lane + 32][t], xt, x1);
     }
     if (lane < nb) A[(int64_t)lane * ld + c] = lane >= c ? x0 : 0.0;
     if (lane + 32 < nb) A[(int64_t)(lane + 32) * ld + c] = lane + 32 >= c ? x1 : 0.0;
@@ -293,18 +302,10 @@ __global__ void __launch_bounds__(256) potf2_inv_kernel(double* A, int64_t ld, i
 // over blockIdx.z.  op(B)[k, n] = transB ? B[n, k] : B[k, n].  Triangular
 // operands restrict the k range per tile: triA (A lower) k < m0 + 64;
 // triB (B lower as stored) k >= n0 without transB, k < n0 + 64 with it.
-// lowerC skips tiles strictly above the diagonal.  M, N multiples of 64,
-// the k range a multiple of 16; every offset fits in 32 bits (N <= 32768).
-// C must not alias A or B.
-//
-// 256 threads, 4x4 outputs per thread (rows 2ty, 2ty+1, 32+2ty, 33+2ty and
-// the same pattern of columns in tx), 16-deep k chunks: the next chunk is
-// loaded into registers while the current one is multiplied out of shared
-// memory (two buffers, one barrier per chunk).  Shared tiles are k-major
-// [k][64] with element (k, j) at column j ^ k, so the coalesced global
-// loads (16 consecutive k per row) store without bank conflicts and each
-// thread's aligned pairs stay pairs (read as one 16-byte load, swapped back
-// in registers when k is odd).
+// lowerC skips tiles strictly above the diagonal and leaves the strict upper
+// triangle of diagonal tiles untouched.  M, N multiples of 64, the k range a
+// multiple of 16; every offset fits in 32 bits (N <= 32768).  C must not
+// alias A or B.
 struct DGemm {
   const double* A;
   const double* B;
@@ -314,7 +315,14 @@ struct DGemm {
   double alpha;
 };
 
-__global__ void __launch_bounds__(256, 2) dgemm_kernel(DGemm g) {
+// The GEMM on the fp64 tensor cores (mma.sync m8n8k4 f64; tcgen05 has no
+// fp64 kind): 64x64 tiles, 4 warps of 32x32 (4x4 fragments of 8x8), 16-deep
+// k chunks double-buffered through registers.  A is staged row-major [m][20] (k inner), B
+// row-major [n][20] with transB and k-major [k][68] without; the strides
+// make the fragment reads (8 rows x 4 k per warp) and the coalesced stores
+// free of bank conflicts.
+template <bool TRANSB>
+__global__ void __launch_bounds__(128, 3) dgemm_mma_kernel(DGemm g) {
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   if (g.lowerC && m0 + 64 <= n0) return;
   const double* __restrict__ A = g.A + (int64_t)blockIdx.z * g.sA;
@@ -324,86 +332,94 @@ __global__ void __launch_bounds__(256, 2) dgemm_kernel(DGemm g) {
   int k0 = 0, k1 = g.K;
   if (g.triA) k1 = min(k1, m0 + 64);
   if (g.triB) {
-    if (g.transB) k1 = min(k1, n0 + 64);
+    if (TRANSB) k1 = min(k1, n0 + 64);
     else k0 = n0;
   }
-  __shared__ __align__(16) double As[2][16][64];
-  __shared__ __align__(16) double Bs[2][16][64];
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  // load slots: A rows (tid >> 4) + 16 r, k = tid & 15; B likewise (transB) or k = tid >> 6 + 4 r, n = tid & 63
-  const int lk = tid & 15, lm = tid >> 4;
-  const int bk = tid >> 6, bn = tid & 63;
-  double ra[4], rb[4];
+  constexpr int SA = 20;                 // [64][SA]
+  constexpr int SBK = TRANSB ? 20 : 68;  // transB: [64 n][20]; else [16 k][68]
+  constexpr int BSZ = TRANSB ? 64 * 20 : 16 * 68;
+  __shared__ __align__(16) double As[2][64 * SA];
+  __shared__ __align__(16) double Bs[2][BSZ];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+  // loads: 64 x 16 doubles per operand, 8 per thread
+  const int lk = tid & 15, lr = tid >> 4;  // k-contiguous: rows lr + 8 r
+  const int bn = tid & 63, bk = tid >> 6;  // n-contiguous: k rows bk + 2 r
+  double ra[8], rb[8];
   auto gload = [&](int kb) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) ra[r] = A[(m0 + lm + 16 * r) * lda + kb + lk];
-    if (g.transB) {
+    for (int r = 0; r < 8; ++r) ra[r] = A[(m0 + lr + 8 * r) * lda + kb + lk];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) rb[r] = B[(n0 + lm + 16 * r) * ldb + kb + lk];
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) rb[r] = B[(kb + bk + 4 * r) * ldb + n0 + bn];
+    for (int r = 0; r < 8; ++r) {
+      if (TRANSB) rb[r] = B[(n0 + lr + 8 * r) * ldb + kb + lk];
+      else rb[r] = B[(kb + bk + 2 * r) * ldb + n0 + bn];
     }
   };
   auto sstore = [&](int buf) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) As[buf][lk][(lm + 16 * r) ^ lk] = ra[r];
-    if (g.transB) {
+    for (int r = 0; r < 8; ++r) As[buf][(lr + 8 * r) * SA + lk] = ra[r];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) Bs[buf][lk][(lm + 16 * r) ^ lk] = rb[r];
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) Bs[buf][bk + 4 * r][bn ^ (bk + 4 * r)] = rb[r];
+    for (int r = 0; r < 8; ++r) {
+      if (TRANSB) Bs[buf][(lr + 8 * r) * SBK + lk] = rb[r];
+      else Bs[buf][(bk + 2 * r) * SBK + bn] = rb[r];
     }
   };
-  double acc[4][4];
+  double acc[4][4][2];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
   if (k0 < k1) {
     gload(k0);
     sstore(0);
   }
   __syncthreads();
+  const int fr = lane >> 2, fk = lane & 3;  // fragment row / k of this lane
   int buf = 0;
   for (int kb = k0; kb < k1; kb += 16) {
     const bool more = kb + 16 < k1;
     if (more) gload(kb + 16);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int pa = (ty * 2) ^ (k & 14), pb = (tx * 2) ^ (k & 14);
-      const double2 a01 = *reinterpret_cast<const double2*>(&As[buf][k][pa]);
-      const double2 a23 = *reinterpret_cast<const double2*>(&As[buf][k][pa + 32]);
-      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[buf][k][pb]);
-      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[buf][k][pb + 32]);
-      const bool sw = k & 1;
-      const double av[4] = {sw ? a01.y : a01.x, sw ? a01.x : a01.y, sw ? a23.y : a23.x, sw ? a23.x : a23.y};
-      const double bv[4] = {sw ? b01.y : b01.x, sw ? b01.x : b01.y, sw ? b23.y : b23.x, sw ? b23.x : b23.y};
+    for (int kk = 0; kk < 16; kk += 4) {
+      double af[4], bf[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) af[i] = As[buf][(wm + i * 8 + fr) * SA + kk + fk];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        bf[j] = TRANSB ? Bs[buf][(wn + j * 8 + fr) * SBK + kk + fk] : Bs[buf][(kk + fk) * SBK + wn + j * 8 + fr];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j)
+          asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                       : "+d"(acc[i][j][0]), "+d"(acc[i][j][1])
+                       : "d"(af[i]), "d"(bf[j]));
     }
     if (more) sstore(buf ^ 1);
     __syncthreads();
     buf ^= 1;
   }
+  // accumulator fragment: row fr, columns 2 fk + {0, 1} of each 8x8 tile
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    double* c = C + (m0 + (i < 2 ? 0 : 32) + ty * 2 + (i & 1)) * ldc + n0 + tx * 2;
+    const int row = m0 + wm + i * 8 + fr;
+    double* c = C + row * ldc;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      double* cj = c + (j < 2 ? 0 : 32) + (j & 1);
-      *cj = g.accumulate ? fma(g.alpha, acc[i][j], *cj) : g.alpha * acc[i][j];
-    }
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = n0 + wn + j * 8 + 2 * fk + e;
+        if (g.lowerC && col > row) continue;
+        c[col] = g.accumulate ? fma(g.alpha, acc[i][j][e], c[col]) : g.alpha * acc[i][j][e];
+      }
   }
 }
 
 int dgemm(const DGemm& g, int batch, cudaStream_t st) {
   dim3 grid((unsigned)(g.N / 64), (unsigned)(g.M / 64), (unsigned)batch);
-  dgemm_kernel<<<grid, 256, 0, st>>>(g);
-  return check_cuda(cudaGetLastError(), "dgemm_kernel launch");
+  if (g.transB) dgemm_mma_kernel<true><<<grid, 128, 0, st>>>(g);
+  else dgemm_mma_kernel<false><<<grid, 128, 0, st>>>(g);
+  return check_cuda(cudaGetLastError(), "dgemm_mma_kernel launch");
 }
 
 // ----------------------------------------------------------------------------
@@ -633,6 +649,8 @@ namespace {
 //   X22 = chol_inv(A22); X21 = -(X22 L21) X11 (through t3).
 // Every GEMM is h x h x h with the triangular operand's zero tiles skipped;
 // the 64-wide leaves are factored and inverted by potf2_inv_kernel.
+constexpr size_t POTF2_SMEM = sizeof(double) * (2 * PB * (PB + 1) + PB);
+
 struct HinvCtx {
   double* A;
   int64_t N;
@@ -646,7 +664,7 @@ int chol_inv(const HinvCtx& c, int64_t off, int64_t n, int level) {
   const int64_t N = c.N;
   double* A11 = c.A + off * (N + 1);
   if (n <= PB) {
-    potf2_inv_kernel<<<1, 256, sizeof(double) * PB * (PB + 1), c.st>>>(A11, N, (int)n, off, c.info);
+    potf2_inv_kernel<<<1, 256, POTF2_SMEM, c.st>>>(A11, N, (int)n, off, c.info);
     return check_cuda(cudaGetLastError(), "potf2_inv_kernel launch");
   }
   const int64_t h = n / 2;
@@ -693,7 +711,7 @@ extern "C" int qi8_hinv_upper(double* h_rev, int64_t N, float* hinv_out, int* in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = check_cuda(cudaMemsetAsync(info, 0, sizeof(int), st), "cudaMemsetAsync");
   if (rc != QI8_OK) return rc;
-  rc = set_smem((const void*)potf2_inv_kernel, sizeof(double) * PB * (PB + 1));
+  rc = set_smem((const void*)potf2_inv_kernel, POTF2_SMEM);
   if (rc != QI8_OK) return rc;
   HinvCtx c{};
   c.A = h_rev;
