@@ -6,6 +6,7 @@
     python benchmarks/microbench.py gemm_stack  # K2 on the Flux / T5 stacks' largest linears
     python benchmarks/microbench.py convert  # K4 QuIP conversion
     python benchmarks/microbench.py ldlq     # default converter: fp64 Hinv factorization, LDLQ pass
+    python benchmarks/microbench.py gemm_ksweep  # K2 plain GEMM over K at fixed M, N
 
 Each case is timed with CUDA events around one launch, median of ``--iters``
 launches, with a 256 MB buffer rewritten between launches so every launch
@@ -197,9 +198,28 @@ def ldlq_cases(run, dev):
     return res
 
 
+def gemm_ksweep_cases(run, dev):
+    """The plain-scale per-row GEMM with bf16 bias and output at fixed M, N
+    over K (a per-tile floor shows as time that stops falling with K)."""
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    for M, N, K in [(4608, 21504, 1536), (4608, 21504, 3072), (4608, 21504, 6144), (4608, 21504, 12288),
+                    (4096, 12288, 3072), (4608, 3072, 15360)]:
+        a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        xs = torch.rand(M, 1, device=dev, generator=g) * 0.01
+        ws = torch.rand(N, device=dev, generator=g) * 0.01
+        bias = torch.randn(N, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        us = run(lambda: ops.gemm_i8(a, b, xs, L.QI8_S_ROW, ws, L.QI8_S_ROW, bias, torch.bfloat16, out=out))
+        res[f"k2_plain_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
+        del a, b, out
+    return res
+
+
 CASES = {"rotate": rotate_cases, "quant": quant_cases, "gemm": gemm_cases, "gemm_stack": gemm_stack_cases,
          "gemm_tile": gemm_tile_cases,
-         "convert": convert_cases, "ldlq": ldlq_cases}
+         "convert": convert_cases, "ldlq": ldlq_cases, "gemm_ksweep": gemm_ksweep_cases}
 
 
 def main(argv=None):

@@ -510,6 +510,38 @@ __device__ __forceinline__ float row_scale(const float* s, int kind, int m) {
   return 1.0f;
 }
 
+// Plain-scale epilogue of 32 consecutive output columns of one row
+// (optimized_linear, comfy/quant_ops.py:472-474):
+//   y[j] = float(acc[j]) * (frow * col[j]) + bias[j], then the optional GELU,
+// every operation separately rounded.  col / bias are this warp's staged
+// column scales and bias (16-byte aligned, read as vectors); the GELU runs
+// as its own pass so the scale loop stays branch-free -- with the GELU test
+// inside it every unrolled element carried the inlined GELU code, and that
+// epilogue, not the MMAs, set the pace of short-K GEMMs.
+__device__ __forceinline__ void plain_epilogue32(const uint32_t (&acc)[32], float frow, const float* col,
+                                                 const float* bias, bool has_bias, int act, int out_dtype,
+                                                 float (&y)[32]) {
+  const float4* c4 = reinterpret_cast<const float4*>(col);
+  const float4* b4 = reinterpret_cast<const float4*>(bias);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 s = c4[q];
+    const float sv[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) y[4 * q + u] = __fmul_rn(__int2float_rn((int)acc[4 * q + u]), __fmul_rn(frow, sv[u]));
+    if (has_bias) {
+      const float4 b = b4[q];
+      const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) y[4 * q + u] = __fadd_rn(y[4 * q + u], bv[u]);
+    }
+  }
+  if (act == QI8_ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = act_gelu(y[j], out_dtype);
+  }
+}
+
 // Tile epilogue of the block-scaled kernels: final scales, optional GELU and
 // the stores, from the WC accumulator registers of one thread.
 // SWAP: thread = output feature rr, the 128 values are tokens cc0..cc0+127;
@@ -1026,13 +1058,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               store_row32_i32(p, m, n0, r[c]);
             } else {
               float y[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                // optimized_linear: res.float() * (x_s * w_s) + bias  (comfy/quant_ops.py:472-473)
-                y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(fa, my_col[cc + j]));
-                if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
-                if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
-              }
+              plain_epilogue32(r[c], fa, my_col + cc, my_bias + cc, p.bias != nullptr, p.act, p.out_dtype, y);
               store_row32_t<MULTI>(p, e, m, n0, y);
             }
           }
@@ -1485,12 +1511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               // memory so that each store writes 64 contiguous bytes of a row
               if (n0 < p.N && n0 + 32 <= p.N && p.out_dtype != QI8_F32) {  // warp-uniform
                 float y[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(frow, my_col[cc + j]));
-                  if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
-                  if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
-                }
+                plain_epilogue32(r[c], frow, my_col + cc, my_bias + cc, p.bias != nullptr, p.act, p.out_dtype, y);
                 store_tile32_multi(p, e, reinterpret_cast<uint4*>(sxp + warp * (2 * 16 * 32)), rr - lane, R, n0,
                                    y, lane);
                 continue;
@@ -1501,13 +1522,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               store_row32_i32(p, rr, n0, r[c], plane);
             } else {
               float y[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                // optimized_linear: res.float() * (x_s * w_s) + bias  (comfy/quant_ops.py:472-473)
-                y[j] = __fmul_rn(__int2float_rn((int)r[c][j]), __fmul_rn(frow, my_col[cc + j]));
-                if (p.bias) y[j] = __fadd_rn(y[j], my_bias[cc + j]);
-                if (p.act == QI8_ACT_GELU) y[j] = act_gelu(y[j], p.out_dtype);
-              }
+              plain_epilogue32(r[c], frow, my_col + cc, my_bias + cc, p.bias != nullptr, p.act, p.out_dtype, y);
               store_row32_t<MULTI>(p, e, rr, n0, y);
             }
           }
