@@ -1676,7 +1676,10 @@ __global__ void splitk_finalize_kernel(const int32_t* __restrict__ ws, int S, in
     for (int j = 0; j < 4; ++j) {
       y[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(fr, row_scale(b_scale, b_kind, n + j)));
       if (bias) y[j] = __fadd_rn(y[j], load_as_f32(bias, bias_dtype, n + j));
-      if (act == QI8_ACT_GELU) y[j] = act_gelu(y[j], out_dtype);
+    }
+    if (act == QI8_ACT_GELU) {  // its own pass, as in plain_epilogue32
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = act_gelu(y[j], out_dtype);
     }
     if (out_dtype == QI8_F32) {
       *reinterpret_cast<float4*>(static_cast<float*>(out) + o) = make_float4(y[0], y[1], y[2], y[3]);
