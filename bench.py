@@ -802,7 +802,7 @@ def main_dit_mlp(args):
 def main_quip_linear(args):
     """Config 1: one QuIP W8A8 linear in transformed storage (tensorwise
     scale): x [512, 4096] -> K1 (signs + FWHT + per-token int8) -> K2 (int8
-    GEMM, fp32 out; split over K when its tiles fill few SMs) -> K3 (FWHT +
+    GEMM, fp32 out; split over K when its tiles fill few SMs and K is long) -> K3 (FWHT +
     signs + bias -> bf16).  The step is captured once as a CUDA graph."""
     from convert_to_quant_quip_int8_b200 import _lib as L
     from convert_to_quant_quip_int8_b200 import ops

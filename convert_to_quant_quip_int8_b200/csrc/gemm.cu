@@ -1698,13 +1698,18 @@ __global__ void splitk_finalize_kernel(const int32_t* __restrict__ ws, int S, in
 }
 
 // K splits of a plain-scale GEMM on the pair kernel: only when its tiles
-// fill at most half of the co-resident CTA pairs and K has >= 8 blocks per
-// split... returns the number of splits (1 = none) and the blocks per split.
+// fill at most half of the co-resident CTA pairs, K has >= 64 blocks
+// (K >= 8192) and every split keeps >= 8 blocks.  Measured as device time
+// under graph replay, splitting lost 0.5-5 us at K = 3072 and 4096 (the
+// unsplit tile is ~14 us there, and the int32 planes plus the reduce cost
+// more than the shorter main loop saves) and won from K = 12288 up
+// (64 x 3072 x 12288: 20.6 against 40.7 us).  Returns the number of splits
+// (1 = none) and the blocks per split.
 int choose_splits(int64_t Rrows, int64_t Crows, int64_t K, int max_clusters, int* kb_split) {
   const int KB = (int)((K + BK - 1) / BK);
   *kb_split = KB;
   const int64_t tiles = ((Rrows + 255) / 256) * ((Crows + pairk::PBN - 1) / pairk::PBN);
-  if (max_clusters <= 0 || tiles * 2 > max_clusters || KB < 16) return 1;
+  if (max_clusters <= 0 || tiles * 2 > max_clusters || KB < 64) return 1;
   int s = (int)(max_clusters / tiles);
   if (s > 8) s = 8;
   if (s > KB / 8) s = KB / 8;

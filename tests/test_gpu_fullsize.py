@@ -12,7 +12,7 @@ with the CPU oracle on the same seeded inputs:
   partials are exact; only the fp32 summation order differs), bf16 within
   1e-2, and the int32 accumulators of both shapes bit-exact;
 * the single QuIP linear (512 x 4096 -> 4096, transformed storage):
-  K1 -> K2 (split over K) -> K3, every stage bit-exact;
+  K1 -> K2 -> K3, every stage bit-exact;
 * one Flux single-block linear (4608 x 3072 -> 21504, per-row scale, bias)
   and one T5-XXL wi linear (4096 x 10240 -> 4096, axis-wise scale):
   per-token int8, int32 accumulator and bf16 output bit-exact.
@@ -114,8 +114,8 @@ def test_dit_block_gemm_fullsize(dit, which):
 
 def test_quip_linear_config1_fullsize():
     """Config 1 at full size: x [512, 4096], W' [4096, 4096] transformed
-    storage; K1 (signs + FWHT + per-token int8), K2 (fp32 out, K split in two
-    through the caller workspace), K3 (FWHT + signs + bias -> bf16)."""
+    storage; K1 (signs + FWHT + per-token int8), K2 (fp32 out), K3 (FWHT +
+    signs + bias -> bf16)."""
     wl = SingleQuipLinear()
     su, sv = wl.signs()
     q, s, _ = ops.quip_convert(wl.weight().to(dev()), su, sv, store_transformed=True, want_dequant=False)

@@ -23,9 +23,11 @@ def _unsplit(a, b, a_s, a_kind, b_s, b_kind, bias, dtype, act):
     return out
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (300, 512, 2048), (129, 1024, 8192),
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 8192), (300, 512, 8192), (129, 1024, 8192),
                                    # rows <= 128 take the CTA-pair kernel when they split (zero-filled rows)
-                                   (64, 3072, 12288), (37, 1024, 4096), (1, 512, 2048),
+                                   (64, 3072, 12288), (37, 1024, 9216), (1, 512, 8192),
+                                   # a last split shorter than the others, its last K block partial
+                                   (200, 1024, 8208),
                                    # per-rank shapes of the Flux stack split over 8 GPUs
                                    (576, 3072, 15360), (512, 3072, 12288)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
@@ -49,7 +51,7 @@ def test_split_k_equals_unsplit(M, N, K, dtype, kind):
 
 
 def test_split_k_int32_equals_oracle():
-    M, N, K = 512, 2048, 4096
+    M, N, K = 512, 2048, 8192
     r = np.random.default_rng(5)
     a = r.integers(-128, 128, (M, K), dtype=np.int8)
     b = r.integers(-128, 128, (N, K), dtype=np.int8)
@@ -61,4 +63,8 @@ def test_split_k_int32_equals_oracle():
 def test_split_decision_by_grid_and_scales():
     assert ops._gemm_ws_bytes(4096, 12288, 3072, L.QI8_S_ROW, L.QI8_S_ROW) == 0
     assert ops._gemm_ws_bytes(512, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW_KBLOCK) == 0
-    assert ops._gemm_ws_bytes(64, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW) > 0  # few rows, few tiles: splits
+    # few rows, few tiles: splits only when K is long enough to pay for the reduce
+    assert ops._gemm_ws_bytes(64, 4096, 4096, L.QI8_S_ROW, L.QI8_S_ROW) == 0
+    assert ops._gemm_ws_bytes(64, 3072, 3072, L.QI8_S_ROW, L.QI8_S_ROW) == 0
+    assert ops._gemm_ws_bytes(64, 4096, 8192, L.QI8_S_ROW, L.QI8_S_ROW) > 0
+    assert ops._gemm_ws_bytes(576, 3072, 15360, L.QI8_S_ROW, L.QI8_S_ROW) > 0
