@@ -14,6 +14,12 @@ whole forward can be captured once and replayed as a CUDA graph.
   8 x 512 tokens; axis-wise weight scales ``[N]``
   (``AxisWiseINT8Layout``, comfy/quant_ops.py:330-339).
 
+Independent linears overlap: a double block's txt linears (and T5's k next
+to q and v, wi_1 next to wi_0) run on a second stream of the captured graph,
+forked at the start of their group and joined at its end, with their own
+quantization, workspace and output buffers.  Small per-rank GEMMs of a token
+split fill few CTA pairs, so the other lane's GEMM runs on the idle SMs.
+
 Each linear is the reference's W8A8 forward (comfy/quant_ops.py:461-475):
 per-token int8 quantization of the bf16 input (K1), then the int8 GEMM with
 the fused ``acc * (x_s * w_s) + bias`` epilogue (K2) to bf16.  Inputs are
@@ -57,20 +63,33 @@ class LinearSpec:
     n: int
     src: str = "x"      # "x": synthetic activation [tokens, k]; otherwise the linear whose output feeds this one
     gelu: bool = False  # GELU of the input, fused into the per-token quantization
+    lane: int = 0       # 1: runs on the second stream, concurrently with lane 0 of its group
+    group: str = ""     # consecutive specs of one non-empty group fork at its start and join at its end
 
 
 def flux_specs() -> List[LinearSpec]:
     specs = []
     for name, t, k, n in flux_linears():
+        # a double block's txt linears are independent of its img linears
+        lane = 1 if ".txt." in name else 0
+        group = name.split(".")[0] if name.startswith("double") else ""
         if name.endswith(".mlp2"):
-            specs.append(LinearSpec(name, t, k, n, name[: -len("mlp2")] + "mlp0", True))
+            specs.append(LinearSpec(name, t, k, n, name[: -len("mlp2")] + "mlp0", True, lane, group))
         else:
-            specs.append(LinearSpec(name, t, k, n))
+            specs.append(LinearSpec(name, t, k, n, lane=lane, group=group))
     return specs
 
 
 def t5_specs() -> List[LinearSpec]:
-    return [LinearSpec(name, t, k, n) for name, t, k, n in t5_linears()]
+    # q, k, v read the same input; so do wi_0 and wi_1
+    lane = {"k": 1, "wi_1": 1}
+    group = {"q": "qkv", "k": "qkv", "v": "qkv", "wi_0": "wi", "wi_1": "wi"}
+    specs = []
+    for name, t, k, n in t5_linears():
+        pre, part = name.split(".")
+        g = f"{pre}.{group[part]}" if part in group else ""
+        specs.append(LinearSpec(name, t, k, n, lane=lane.get(part, 0), group=g))
+    return specs
 
 
 STACKS = {
@@ -83,6 +102,19 @@ STACKS = {
 }
 
 
+def fork_groups(specs: List[LinearSpec]) -> List[Tuple[List[int], bool]]:
+    """Consecutive specs of one non-empty group form a group; every other
+    spec is a group of its own.  Returns (spec indices, forks) per group in
+    order, where ``forks`` says whether the group has lane-1 linears."""
+    groups: List[List[int]] = []
+    for i, sp in enumerate(specs):
+        if groups and sp.group and specs[i - 1].group == sp.group:
+            groups[-1].append(i)
+        else:
+            groups.append([i])
+    return [(ix, any(specs[j].lane for j in ix)) for ix in groups]
+
+
 def ops_per_forward(specs: List[LinearSpec]) -> int:
     return sum(2 * s.tokens * s.k * s.n for s in specs)
 
@@ -92,7 +124,8 @@ class LinearStack:
     shard), synthetic inputs and every intermediate buffer, preallocated."""
 
     def __init__(self, name: str, device: torch.device, rank: int = 0, world: int = 1, shard: str = "replica",
-                 chunks: int = 4, group=None, specs: Optional[List[LinearSpec]] = None, gather: str = "peer"):
+                 chunks: int = 4, group=None, specs: Optional[List[LinearSpec]] = None, gather: str = "peer",
+                 overlap: bool = True):
         cfg = STACKS[name]
         self.name, self.cfg, self.device = name, cfg, device
         self.specs = cfg["specs"]() if specs is None else list(specs)
@@ -100,9 +133,15 @@ class LinearStack:
             # token split: full weights on every rank, each rank its 1/G of every linear's tokens
             for sp in self.specs:
                 assert sp.tokens % world == 0, f"{sp.name}: {sp.tokens} tokens do not split over {world} ranks"
-            self.specs = [LinearSpec(sp.name, sp.tokens // world, sp.k, sp.n, sp.src, sp.gelu) for sp in self.specs]
+            self.specs = [LinearSpec(sp.name, sp.tokens // world, sp.k, sp.n, sp.src, sp.gelu, sp.lane, sp.group)
+                          for sp in self.specs]
         self.rank, self.world, self.group = rank, world, group
         self.sharded = shard == "columns" and world > 1
+        # the second stream only where lanes exist and no collective orders the linears
+        self.overlap = overlap and not self.sharded and any(sp.lane for sp in self.specs)
+        self.side = torch.cuda.Stream(device) if self.overlap else None
+        self.groups = fork_groups(self.specs) if self.overlap else [([i], False) for i in range(len(self.specs))]
+        self.fork_events = [(torch.cuda.Event(), torch.cuda.Event()) for ix, f in self.groups if f]
         self.chunks = chunks
         self.gather = gather  # column mode: "peer" (fused into the GEMM epilogue) or "nccl"
         self.peer = None
@@ -160,62 +199,82 @@ class LinearStack:
                     g = torch.Generator(device=dev)
                     g.manual_seed(seed)
                     self.inputs[key] = torch.randn(s.tokens, s.k, generator=g, device=dev).to(torch.bfloat16)
-        max_tk = max(s.tokens * s.k for s in self.specs)
-        max_t = max(s.tokens for s in self.specs)
         max_tn = max(s.tokens * s.n for s in self.specs)
-        self.xq = torch.empty(max_tk, dtype=torch.int8, device=dev)
-        self.xs = torch.empty(max_t, dtype=torch.float32, device=dev)
-        # split-K workspace: GEMMs whose output tiles fill few CTA pairs (the
-        # small token counts of a token split, or a thin output) split K into
-        # exact int32 partial planes reduced by a second pass
-        self.ws_bytes = 0
-        if not self.sharded:
-            self.ws_bytes = max(int(self.lib.qi8_gemm_workspace_bytes(s.tokens, s.n, s.k, L.QI8_S_ROW, L.QI8_S_ROW))
-                                for s in self.specs)
-        self.ws = torch.empty(max(self.ws_bytes, 16), dtype=torch.uint8, device=dev)
-        # consumed outputs get their own buffer per (tokens, n); the rest share a scratch
+        # per lane: quantized activations, their scales, the split-K
+        # workspace (GEMMs whose output tiles fill few CTA pairs split K into
+        # exact int32 partial planes reduced by a second pass) and an output
+        # scratch; lane 0's are also the attributes xq, xs, ws, scratch
+        self.lane_bufs: Dict[int, Dict[str, object]] = {}
+        for ln in sorted({self.lane(s) for s in self.specs}):
+            mine = [s for s in self.specs if self.lane(s) == ln]
+            ws_bytes = 0
+            if not self.sharded:
+                ws_bytes = max(int(self.lib.qi8_gemm_workspace_bytes(s.tokens, s.n, s.k, L.QI8_S_ROW, L.QI8_S_ROW))
+                               for s in mine)
+            self.lane_bufs[ln] = {
+                "xq": torch.empty(max(s.tokens * s.k for s in mine), dtype=torch.int8, device=dev),
+                "xs": torch.empty(max(s.tokens for s in mine), dtype=torch.float32, device=dev),
+                "ws": torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev),
+                "ws_bytes": ws_bytes,
+            }
+        b0 = self.lane_bufs[0] if 0 in self.lane_bufs else next(iter(self.lane_bufs.values()))
+        self.xq, self.xs, self.ws, self.ws_bytes = b0["xq"], b0["xs"], b0["ws"], b0["ws_bytes"]
+        # consumed outputs get their own buffer per (lane, tokens, n); the rest share their lane's scratch
         keys = []
         for s in self.specs:
-            if s.name in consumed and (s.tokens, s.n) not in keys:
-                keys.append((s.tokens, s.n))
+            key = (self.lane(s), s.tokens, s.n)
+            if s.name in consumed and key not in keys:
+                keys.append(key)
         if self.sharded and self.gather == "peer":
             # every output lives in a peer-mapped buffer: the scratch is buffer 0, kept outputs follow
             self.peer = PeerWorkspace(max_tn * 2, self.world, self.rank, self.group, 1 + len(keys), dev)
             self.peer_index = {k: 1 + i for i, k in enumerate(keys)}
-            self.kept = {k: self.peer.buffer(1 + i, k, torch.bfloat16) for i, k in enumerate(keys)}
-            self.scratch = self.peer.bufs[0].view(torch.bfloat16)
+            self.kept = {k: self.peer.buffer(1 + i, k[1:], torch.bfloat16) for i, k in enumerate(keys)}
+            self.lane_bufs[0]["scratch"] = self.peer.bufs[0].view(torch.bfloat16)
         else:
-            self.kept = {k: torch.empty(*k, dtype=torch.bfloat16, device=dev) for k in keys}
-            self.scratch = torch.empty(max_tn, dtype=torch.bfloat16, device=dev)
+            self.kept = {k: torch.empty(*k[1:], dtype=torch.bfloat16, device=dev) for k in keys}
+            for ln, lb in self.lane_bufs.items():
+                lb["scratch"] = torch.empty(max(s.tokens * s.n for s in self.specs if self.lane(s) == ln),
+                                            dtype=torch.bfloat16, device=dev)
+        self.scratch = b0["scratch"]
         self.out_of = {}
         for s in self.specs:
-            buf = self.kept.get((s.tokens, s.n)) if s.name in consumed else None
-            self.out_of[s.name] = buf if buf is not None else self.scratch[: s.tokens * s.n].view(s.tokens, s.n)
-        self.buf_index = {s.name: (self.peer_index[(s.tokens, s.n)] if self.peer is not None and s.name in consumed
+            key = (self.lane(s), s.tokens, s.n)
+            buf = self.kept.get(key) if s.name in consumed else None
+            scratch = self.lane_bufs[self.lane(s)]["scratch"]
+            self.out_of[s.name] = buf if buf is not None else scratch[: s.tokens * s.n].view(s.tokens, s.n)
+        self.buf_index = {s.name: (self.peer_index[(0, s.tokens, s.n)] if self.peer is not None and s.name in consumed
                                    else 0) for s in self.specs}
         if self.sharded and self.gather == "nccl":
             max_tnl = max(s.tokens * (s.n // self.world) for s in self.specs)
             self.y_loc = torch.empty(max_tnl, dtype=torch.bfloat16, device=dev)
             self.gathered = torch.empty(max_tn, dtype=torch.bfloat16, device=dev)
 
+    def lane(self, s: LinearSpec) -> int:
+        """Stream lane of a linear: its own lane when lanes overlap, else 0."""
+        return s.lane if self.overlap else 0
+
     def source(self, s: LinearSpec) -> torch.Tensor:
         return self.inputs[(s.tokens, s.k)] if s.src == "x" else self.out_of[s.src]
 
     # ------------------------------------------------------------ forward
     def _k1(self, x: torch.Tensor, s: LinearSpec, sp):
+        lb = self.lane_bufs[self.lane(s)]
         mode = L.QI8_Q_TOKEN | (L.QI8_Q_GELU if s.gelu else 0)
-        L.check(self.lib.qi8_quant_rows(L.ptr(x), L.QI8_BF16, s.tokens, s.k, s.k, mode, 128, L.ptr(self.xq), s.k,
-                                        L.ptr(self.xs), sp), "qi8_quant_rows")
+        L.check(self.lib.qi8_quant_rows(L.ptr(x), L.QI8_BF16, s.tokens, s.k, s.k, mode, 128, L.ptr(lb["xq"]), s.k,
+                                        L.ptr(lb["xs"]), sp), "qi8_quant_rows")
 
     def _gemm(self, i: int, s: LinearSpec, lo: int, hi: int, out_ptr: int, ld_out: int, sp):
         q, sc, bias = self.weights[i]
+        lb = self.lane_bufs[self.lane(s)]
         n = q.shape[0]
-        a = self.xq.data_ptr() + lo * s.k
-        xs = self.xs.data_ptr() + lo * 4
+        a = lb["xq"].data_ptr() + lo * s.k
+        xs = lb["xs"].data_ptr() + lo * 4
         L.check(self.lib.qi8_gemm_i8_ws(ctypes.c_void_p(a), L.ptr(q), hi - lo, n, s.k, ctypes.c_void_p(xs),
                                         L.QI8_S_ROW, L.ptr(sc), L.QI8_S_ROW, L.ptr(bias),
                                         L.QI8_BF16 if bias is not None else 0, ctypes.c_void_p(out_ptr), L.QI8_BF16,
-                                        ld_out, L.QI8_ACT_NONE, L.ptr(self.ws), self.ws_bytes, sp), "qi8_gemm_i8_ws")
+                                        ld_out, L.QI8_ACT_NONE, L.ptr(lb["ws"]), lb["ws_bytes"], sp),
+                "qi8_gemm_i8_ws")
 
     def run_linear(self, i: int, sp, events=None):
         s = self.specs[i]
@@ -257,9 +316,31 @@ class LinearStack:
                     "qi8_gather_layout")
 
     def forward(self, events=None):
+        """One forward on the current stream.  With ``events`` (a start/end
+        event pair per linear around its GEMM launches) every linear runs on
+        the current stream in spec order, so each GEMM is timed alone;
+        otherwise each group with lane-1 linears forks them onto the second
+        stream and joins it at the group's end (graph-capturable)."""
         sp = L.stream_ptr(self.device)
-        for i in range(len(self.specs)):
-            self.run_linear(i, sp, None if events is None else events[i])
+        if events is not None or not self.overlap:
+            for i in range(len(self.specs)):
+                self.run_linear(i, sp, None if events is None else events[i])
+            return
+        main = torch.cuda.current_stream(self.device)
+        side = ctypes.c_void_p(self.side.cuda_stream)
+        forks = iter(self.fork_events)
+        for ix, forked in self.groups:
+            if not forked:
+                for i in ix:
+                    self.run_linear(i, sp)
+                continue
+            fork, join = next(forks)
+            fork.record(main)
+            self.side.wait_event(fork)
+            for i in ix:
+                self.run_linear(i, side if self.specs[i].lane else sp)
+            join.record(self.side)
+            main.wait_event(join)
 
     def launches_per_forward(self) -> int:
         """Kernels of this library launched by one forward (K1 + GEMMs + layouts)."""

@@ -121,3 +121,32 @@ def test_conversion_driver_selects_2d_weights_and_names_shards():
     assert C.weight_keys(shapes) == ["a.weight", "b.lora_A.weight", "c.weight"]
     assert C.weight_keys(shapes, exclude=lambda k: "lora" in k) == ["a.weight", "c.weight"]
     assert C.shard_path("/x/m.safetensors", 1, 4) == "/x/m.safetensors.rank1-of-4"
+
+
+def test_stack_fork_groups():
+    """The Flux stack forks each double block's txt linears onto the second
+    lane (19 groups of 8, the single blocks alone); T5 forks q/k/v and
+    wi_0/wi_1 of every layer; a token split keeps lanes and groups."""
+    from convert_to_quant_quip_int8_b200.stack import LinearSpec, flux_specs, fork_groups, t5_specs
+    fx = flux_specs()
+    g = fork_groups(fx)
+    forked = [ix for ix, f in g if f]
+    assert len(forked) == 19 and all(len(ix) == 8 for ix in forked)
+    assert len(g) == 19 + 76 and sum(len(ix) for ix, _ in g) == 228
+    for ix in forked:
+        names = [fx[i].name for i in ix]
+        assert {fx[i].lane for i in ix if ".txt." in fx[i].name} == {1}
+        assert {fx[i].lane for i in ix if ".img." in fx[i].name} == {0}
+        assert len({n.split(".")[0] for n in names}) == 1
+    # a consumer reads its producer on the same lane
+    by_name = {s.name: s for s in fx}
+    assert all(by_name[s.src].lane == s.lane for s in fx if s.src != "x")
+    t5 = t5_specs()
+    g5 = fork_groups(t5)
+    assert sum(1 for _, f in g5 if f) == 48 and len(g5) == 24 * 4
+    assert [t5[i].name.split(".")[1] for i in g5[0][0]] == ["q", "k", "v"]
+    assert [t5[i].lane for i in g5[0][0]] == [0, 1, 0]
+    # groups only join consecutive specs
+    specs = [LinearSpec("a", 8, 16, 16, group="g"), LinearSpec("b", 8, 16, 16, lane=1, group="g"),
+             LinearSpec("c", 8, 16, 16), LinearSpec("d", 8, 16, 16, lane=1, group="g")]
+    assert fork_groups(specs) == [([0, 1], True), ([2], False), ([3], True)]
