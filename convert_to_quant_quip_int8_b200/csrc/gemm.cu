@@ -103,6 +103,10 @@ struct GemmExt {
   // stores its raw int32 sums to plane s (split_stride elements apart)
   int kb_split;
   int64_t split_stride;
+  // pair-tile width in output columns: 256, or 128 for a plain-scale,
+  // single-output, unsplit GEMM whose 256-wide tiles would fill at most a
+  // quarter of the co-resident CTA pairs (twice the tiles, each half the work)
+  int pbn;
   // Output destinations, each [M, ld_out] from its own base: outs[0] == out
   // on this device; outs[1..n_outs) peer-mapped copies (column-parallel
   // gather), which receive the same tile at the same offset.
@@ -1104,9 +1108,11 @@ constexpr int P_B_BYTES = B_HALF * BK;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;  // 32 KB per CTA
 constexpr int P_STAGES = 6;
 constexpr int P_BUFS = 2;  // TMEM accumulator buffers of 256 columns
-// M = 256 (pair), N = 256
-constexpr uint32_t IDESC_P256 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
-                                ((uint32_t)(256 >> 4) << 24);
+// M = 256 (pair), N = n: s32 accumulator, signed A and B, K-major operands
+__host__ __device__ constexpr uint32_t idesc_pair(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+constexpr uint32_t IDESC_P256 = idesc_pair(256);
 constexpr int P_NUM_BARS = 2 * P_STAGES + 2 * P_BUFS + 1;  // full, empty, tfull, tempty, drain
 constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 2 * 16 * 32 * 2;
 constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + P_SCRATCH + P_NUM_BARS * 8 + 16;
@@ -1237,14 +1243,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             kb_lo = (tile / rc_tiles) * e.kb_split;
             kb_hi = kb_lo + e.kb_split < KB ? kb_lo + e.kb_split : KB;
           }
+          // each CTA loads its 128 rows of the lane operand and half of the
+          // tile's pbn columns of the column operand
+          const int bh = PROMOTE ? B_HALF : e.pbn >> 1;
           const int r0 = (rc % r_ptiles) * 256 + (int)rank * 128;
-          const int c0 = (rc / r_ptiles) * PBN + (int)rank * B_HALF;
+          const int c0 = (rc / r_ptiles) * 2 * bh + (int)rank * bh;
           for (int kb = kb_lo; kb < kb_hi; ++kb) {
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.status, ST_GEMM_PRODUCER, WAIT_LIMIT_NS)) {
               ok = false;
               break;
             }
-            if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * P_STAGE_BYTES);
+            if (leader) mbar_arrive_expect_tx(full_bar(s), 2u * (uint32_t)(P_A_BYTES + bh * BK));
             const uint32_t fb = full0 + (uint32_t)(s * 8);
             tma_load_pair(sA + s * P_A_BYTES, &tmA, kb * BK, r0, fb);
             tma_load_pair(sB + s * P_B_BYTES, &tmB, kb * BK, c0, fb);
@@ -1262,6 +1271,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         int u = 0;  // accumulation units issued (one per K block, or one per tile)
         bool ok = true;
         const int n_units = PROMOTE ? KB : 1;
+        const uint32_t idesc = PROMOTE ? IDESC_P256 : idesc_pair(e.pbn);
         for (int tile = cluster; ok && tile < p.num_tiles; tile += nclusters) {
           for (int w = 0; ok && w < n_units; ++w, ++u) {
             const int buf = u & 1;
@@ -1286,7 +1296,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               const uint64_t db = sw128_desc(sB + s * P_B_BYTES);
 #pragma unroll
               for (int k = 0; k < BK / 32; ++k)
-                mma_pair(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC_P256, (kb > 0 || k > 0) ? 1u : 0u);
+                mma_pair(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
               commit_pair(empty_bar(s), 3);
               if (++s == P_STAGES) {
                 s = 0;
@@ -1324,9 +1334,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         plane = (int64_t)(tile / rc_tiles) * e.split_stride;
       }
       const int rr = (rc % r_ptiles) * 256 + (int)rank * 128 + quad * 32 + lane;
-      const int c0 = (rc / r_ptiles) * PBN;
-      // this warp's 128 accumulator columns (output columns cc0 .. cc0 + 127)
-      const int cc0 = c0 + cg * 128;
+      // this warp's pbn / 2 accumulator columns (output columns cc0 ..)
+      const int half = PROMOTE ? 128 : e.pbn >> 1;
+      const int c0 = (rc / r_ptiles) * 2 * half;
+      const int cc0 = c0 + cg * half;
       const int cc1 = cc0 + 64;
       const bool row_ok = rr < R;
       const bool cols_ok = cc0 < C;
@@ -1490,14 +1501,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int rnd = 0; rnd < 2; ++rnd) {
+        // rounds of 64 columns: two for 256-wide tiles, one for 128-wide
+        const int nrnd = half >> 6;
+#pragma unroll 2
+        for (int rnd = 0; rnd < nrnd; ++rnd) {
           uint32_t r[2][32];
-          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * 128 + rnd * 64);
+          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * half + rnd * 64);
           tmem_ld32(ta, r[0]);
           tmem_ld32(ta + 32, r[1]);
           tmem_wait_ld();
-          if (rnd == 1) {
+          if (rnd == nrnd - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_cluster(tempty0 + (uint32_t)(buf * 8));
@@ -1788,9 +1801,25 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     split_small = S > 1 && workspace_bytes >= (int64_t)S * M * N * 4;
   }
   if (Rrows > BM || split_small) {
-    // CTA pairs: 256 rows on TMEM lanes x 256 columns per pair tile
+    // CTA pairs: 256 rows on TMEM lanes x bnp columns per pair tile.  A
+    // plain GEMM with few tiles splits K (caller workspace, long K), or
+    // else, when even the 128-column tiles fill at most half of the pairs,
+    // halves the tile width so that twice the pairs share the work.  The
+    // narrow tiles cost more L2 traffic and epilogue per multiply-add: a
+    // rule of tiles * 2 <= pairs measured slower on the linear stacks,
+    // whose second stream's GEMM runs on the pairs a lone GEMM leaves idle.
+    int S = 1, kb_split = (int)((K + BK - 1) / BK);
+    if (!promote && n_outs == 1 && workspace && aligned16(workspace)) {
+      S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
+      if (S > 1 && workspace_bytes < (int64_t)S * M * N * 4) S = 1;
+    }
+    int bnp = pairk::PBN;
+    if (S == 1 && !promote && n_outs == 1) {
+      const int64_t tiles = ((Rrows + 255) / 256) * ((Crows + pairk::PBN - 1) / pairk::PBN);
+      const int maxc = pair_max_clusters<false, false, false, false>(dev);
+      if (maxc > 0 && tiles * 4 <= maxc) bnp = pairk::PBN / 2;
+    }
     GemmArgs p{};
-    const int bnp = pairk::PBN;
     p.M = (int)M; p.N = (int)N; p.K = (int)K; p.KB = (int)((K + BK - 1) / BK);
     p.r_tiles = (int)((Rrows + 255) / 256);
     p.c_tiles = (int)((Crows + bnp - 1) / bnp);
@@ -1805,16 +1834,15 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     p.status = device_status_ptr();
     e.kb_split = p.KB;
     e.split_stride = 0;
+    e.pbn = bnp;
     CUtensorMap mapA, mapB;
     int rc = make_map(&mapA, Rop, Rrows, K, 128);
     if (rc) return rc;
     rc = make_map(&mapB, Cop, Crows, K, bnp / 2);
     if (rc) return rc;
-    if (!promote && n_outs == 1 && workspace) {
+    {
       // few tiles: split K over more CTA pairs, int32 partial planes, then one reduce + epilogue pass
-      int kb_split = p.KB;
-      const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
-      if (S > 1 && workspace_bytes >= (int64_t)S * M * N * 4 && aligned16(workspace)) {
+      if (S > 1) {
         GemmArgs q = p;
         GemmExt qe = e;
         qe.kb_split = kb_split;

@@ -467,8 +467,214 @@ int launch(const RotArgs& a, int64_t rows, cudaStream_t st) {
 
 }  // namespace rot2
 
+// ============================== two-phase row FWHT, n = 4096 (K1 per-token)
+// 64 threads per row, 64 elements per thread, so the 12 butterfly stages
+// take two register phases and one trip through shared memory:
+//   phase 0: thread t holds the contiguous run 64t .. 64t+63 and runs the
+//            stages of index bits 0-5;
+//   phase 1: thread t holds t + 64j (j = 0..63) and runs bits 6-11.
+// Stages stay in ascending bit order (the bit-exactness contract of
+// fwht_row.cuh).  The exchange buffer pads each 64-float run to 68 floats,
+// phys(i) = 68 (i >> 6) + (i & 63): the phase-0 128-bit stores (thread t at
+// 68t + 4q, eight threads per wavefront on banks 4(t + q) mod 32) and the
+// phase-1 loads (a warp at 68j + t) are bank-conflict free, and every
+// address is a per-thread base plus an immediate.  The quantized bytes go
+// out in the phase-1 mapping: one byte store per element, a warp writing 32
+// consecutive bytes per store.  The quantization multiply and rounding add
+// stay scalar __fmul_rn/__fadd_rn: a packed f32x2 pair was contracted into
+// one FFMA2 (single rounding), which moves round-half-even ties.
+//
+// Signs: a ±1 sign flips the sign bit of the 16-bit input exactly, so each
+// thread keeps its 64 signs as two bit masks (built once) and XORs them into
+// the raw words -- no per-row sign loads.  Bit p of mask h is the sign of
+// element 32h + 2p, bit 16 + p that of element 32h + 2p + 1, so the masks
+// of word i (elements 2i, 2i + 1) are (mask << (15 - p)) & 0x80008000 with
+// p = i % 16.  A sign vector with any entry other than ±1 takes the
+// multiply path instead (decided per CTA).
+namespace rot64 {
+
+constexpr int L = 12, N = 1 << L, E = 64, P = N / E, PAD = 68;
+constexpr int SMEM = P * PAD * 4;
+
+// butterflies of the six bits of the in-thread index e (stride 1 .. 32):
+// stride 1 pairs sit in one register pair and run as scalar add/sub; the
+// others run on packed pairs (sum, and difference as fma(hi, -1, lo), both
+// single-rounded and identical to the scalar ops)
+__device__ __forceinline__ void stages64(float (&v)[E]) {
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    const float lo = v[e], hi = v[e + 1];
+    v[e] = lo + hi;
+    v[e + 1] = lo - hi;
+  }
+#pragma unroll
+  for (int s = 2; s < E; s <<= 1) {
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      if (!(e & s)) {
+        const float2 lo = make_float2(v[e], v[e + 1]);
+        const float2 hv = make_float2(v[e + s], v[e + s + 1]);
+        const float2 sm = __fadd2_rn(lo, hv);
+        const float2 df = __ffma2_rn(hv, make_float2(-1.0f, -1.0f), lo);
+        v[e] = sm.x;
+        v[e + 1] = sm.y;
+        v[e + s] = df.x;
+        v[e + s + 1] = df.y;
+      }
+    }
+  }
+}
+
+// Per-token int8 of sign(x) FWHT: 16-bit inputs whose width is a multiple
+// of 64 with 16-byte aligned rows (the launcher checks), persistent CTAs of
+// one row at a time; the next row's 128 input bytes per thread are loaded
+// while this row is transformed.
+template <typename T>
+__global__ void __launch_bounds__(P, 8) rot64_quant_kernel(RotArgs a, int64_t rows) {
+  static_assert(sizeof(T) == 2, "16-bit inputs");
+  extern __shared__ float4 dyn_smem[];
+  float* buf = reinterpret_cast<float*>(dyn_smem);
+  __shared__ float red[P / 32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int c0 = t * E;
+  const bool mine = c0 < a.n_in;
+  uint4 raw[8];
+  auto fetch = [&](int64_t r) {
+    if (r < rows && mine) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + r * a.ld_x + c0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) raw[k] = __ldg(p + k);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) raw[k] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  // this thread's signs as bit masks; ±1 everywhere in the CTA or not
+  uint32_t smask[2] = {0u, 0u};
+  bool pm1 = true;
+  if (a.pre_sign && mine) {
+    const float4* sg4 = reinterpret_cast<const float4*>(a.pre_sign + c0);
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) {
+      const float4 s4 = __ldg(sg4 + q);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = 4 * q + u;
+        const float f = u == 0 ? s4.x : (u == 1 ? s4.y : (u == 2 ? s4.z : s4.w));
+        pm1 = pm1 && (f == 1.0f || f == -1.0f);
+        if (f < 0.0f) smask[e >> 5] |= 1u << (((e & 31) >> 1) + 16 * (e & 1));
+      }
+    }
+  }
+  const bool xor_signs = __syncthreads_and(pm1) != 0;
+  fetch(blockIdx.x);
+  float* wrow = buf + t * PAD;  // phase-0 stores
+  const float* rcol = buf + t;  // phase-1 loads
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[E];
+    {
+      if (a.pre_sign && xor_signs) {
+        // recomputed per row: hoisted out of the loop, the 32 word masks
+        // would hold 32 registers
+        asm volatile("" : "+r"(smask[0]), "+r"(smask[1]));
+        // word i = 4k + c of the row's 32 input words
+        auto flip = [&](int i) { return (smask[i >> 4] << (15 - (i & 15))) & 0x80008000u; };
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          raw[k].x ^= flip(4 * k);
+          raw[k].y ^= flip(4 * k + 1);
+          raw[k].z ^= flip(4 * k + 2);
+          raw[k].w ^= flip(4 * k + 3);
+        }
+      }
+      const T* tv = reinterpret_cast<const T*>(raw);
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = Elem<T>::to_f32(tv[e]);
+    }
+    fetch(row + gridDim.x);
+    if (a.pre_sign && !xor_signs && mine) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = __fmul_rn(v[e], __ldg(a.pre_sign + c0 + e));
+    }
+    stages64(v);
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q)
+      *reinterpret_cast<float4*>(wrow + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < E; ++j) v[j] = rcol[PAD * j];
+    stages64(v);
+    float m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) m = fmaxf(m, fabsf(v[e]));
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    // also orders this row's phase-1 loads before the next row's stores
+    __syncthreads();
+    float amax = red[0];
+#pragma unroll
+    for (int w = 1; w < P / 32; ++w) amax = fmaxf(amax, red[w]);
+    // 1/sqrt(4096) = 2^-6 scales exactly: folded into the amax and the
+    // reciprocal, rint(fl(fl(v * 2^-6) * rcp)) == rint(fl(v * (rcp * 2^-6)))
+    // barring subnormal intermediates, which the range test sends to the
+    // unfolded path
+    float nrm = 1.0f;
+    if (a.do_norm) {
+      amax = __fmul_rn(amax, a.norm);
+      if (amax >= 7.8886091e-31f && amax <= 1.2676506e30f) {
+        nrm = a.norm;
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = __fmul_rn(v[e], a.norm);
+      }
+    }
+    const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float rcp = __fmul_rn(__frcp_rn(s), nrm);
+    int8_t* qrow = a.q + row * N + t;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      // rint(fl(v * rcp)) in [-127, 127]: low byte of fl(fl(v * rcp) + 1.5 * 2^23)
+      const float r = __fadd_rn(__fmul_rn(v[j], rcp), 12582912.0f);
+      qrow[P * j] = (int8_t)(__float_as_uint(r) & 0xFF);
+    }
+    if (t == 0) a.scale[row] = s;
+  }
+}
+
+// true when the two-phase kernel takes these arguments: 16-bit rows whose
+// width is a multiple of 64, and enough rows that each persistent CTA
+// walks about two (with one row per CTA its prologue -- sign masks, the
+// unprefetched first row -- is not amortized: 512 rows measured 12.3 us
+// against 10.2 us for the phased kernel; 4096 rows 25.4 against 29.7 us)
+template <typename T>
+bool usable(const RotArgs& a, int64_t rows) {
+  return sizeof(T) == 2 && a.vec != 0 && (a.n_in % E) == 0 && rows >= 2048 &&
+         (!a.pre_sign || (reinterpret_cast<uintptr_t>(a.pre_sign) & 15) == 0);
+}
+
+template <typename T>
+int launch(const RotArgs& a, int64_t rows, cudaStream_t st) {
+  auto kern = rot64_quant_kernel<T>;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, P, SMEM) != cudaSuccess || b < 1) b = 1;
+    per_sm = b;
+  }
+  const int64_t cap = (int64_t)(sm_count() > 0 ? sm_count() : 148) * per_sm;
+  const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+  kern<<<grid, P, SMEM, st>>>(a, rows);
+  return check_cuda(cudaGetLastError(), "rot64_quant_kernel launch");
+}
+
+}  // namespace rot64
+
 template <int L, typename T, int OUT>
 int launch_rotate_L(const RotArgs& a, int64_t rows, cudaStream_t st) {
+  // per-token K1 of 16-bit rows at n = 4096: the two-phase kernel
+  if constexpr (L == rot64::L && OUT == RO_Q_TOKEN && sizeof(T) == 2) {
+    if (rot64::usable<T>(a, rows)) return rot64::launch<T>(a, rows, st);
+  }
   // rows of 2^9 .. 2^14: the phased kernel (vector loads of the pre-signs
   // need them 16-byte aligned); block-128 quantization stays below
   if constexpr (L >= 9 && L <= 14 && OUT != RO_Q_BLOCK) {

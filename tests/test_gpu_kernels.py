@@ -204,6 +204,43 @@ def test_rotate_quant_random(n, n_pad):
     assert np.array_equal(np_(q), qr) and np.array_equal(np_(s), sr)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rotate_quant_two_phase_n4096(dtype):
+    """The two-phase n = 4096 kernel (16-bit rows whose width is a multiple
+    of 64) against the oracle on 2500 rows (several rows per persistent
+    CTA), with outlier channels, an all-zero row and, in bf16, rows whose
+    amax leaves the folded-normalization range; then against the phased
+    kernel (a 3000-wide row takes it) on the same data with and without
+    signs and normalization, and with signs other than +-1."""
+    r = rng(4096)
+    rows, n = 2500, 3072
+    x = r.standard_normal((rows, n)).astype(np.float32)
+    x[:, r.integers(0, n, 8)] *= 30
+    x[3] = 0
+    if dtype == torch.bfloat16:
+        x[5] *= 1e31
+        x[6] *= 1e-34
+    else:
+        x[5] *= 100
+        x[6] *= 1e-3
+    xt = torch.from_numpy(x).to(dtype)
+    sv = (r.integers(0, 2, 4096) * 2 - 1).astype(np.float32)
+    q, s = ops.rotate_quant_rows(xt.to(dev()), cu(sv), 4096)
+    qr, sr = O.rotate_quant_rows(xt.float().numpy(), sv, 4096)
+    assert np.array_equal(np_(q), qr) and np.array_equal(np_(s).reshape(-1), sr.reshape(-1))
+    xz = xt.clone()
+    xz[:, 3000:] = 0
+    # signs other than +-1 take the multiply path instead of the sign-bit flip
+    sw = (sv * r.uniform(0.5, 2.0, 4096)).astype(np.float32)
+    qw, sw_ = ops.rotate_quant_rows(xt.to(dev()), cu(sw), 4096)
+    qwr, swr = O.rotate_quant_rows(xt.float().numpy(), sw, 4096)
+    assert np.array_equal(np_(qw), qwr) and np.array_equal(np_(sw_).reshape(-1), swr.reshape(-1))
+    for sign, norm in ((cu(sv), True), (None, True), (cu(sv), False), (None, False), (cu(sw), True)):
+        q1, s1 = ops.rotate_quant_rows(xz.to(dev()), sign, 4096, normalize=norm)
+        q2, s2 = ops.rotate_quant_rows(xz[:, :3000].contiguous().to(dev()), sign, 4096, normalize=norm)
+        assert torch.equal(q1, q2) and torch.equal(s1, s2), (sign is None, norm)
+
+
 def test_rotate_quant_block_mode():
     r = rng(77)
     x = torch.from_numpy(r.standard_normal((4, 3072)).astype(np.float32)).to(torch.bfloat16)
@@ -293,6 +330,28 @@ def test_gemm_block_rowk_per_token(M, N, K):
     assert rel_fro(np_(y), ref) < 1e-5
     yb = ops.gemm_i8(cu(a), cu(b), cu(sa), L.QI8_S_ROW, cu(sb), L.QI8_S_ROW_KBLOCK, cu(bias), torch.bfloat16)
     assert rel_fro(np_(yb.float()), ref) < REL_BF16
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (300, 1040, 2048), (129, 272, 336), (1000, 1040, 1024),
+                                   (2048, 3072, 3072)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_few_tiles_epilogue_bitexact(M, N, K, dtype):
+    """Plain per-row GEMMs whose 256-column pair tiles would fill at most a
+    quarter of the CTA pairs run 128-column tiles (ragged last tile at
+    N = 1040); 512 x 4096 (32 tiles) and 2048 x 3072 keep 256-column tiles.
+    Output with bias is bit-exact against the oracle's W8A8 epilogue."""
+    r = rng(M + 3 * N + K)
+    a = r.integers(-128, 128, (M, K), dtype=np.int8)
+    b = r.integers(-127, 128, (N, K), dtype=np.int8)
+    sa = (r.random((M, 1)) * 0.01 + 1e-3).astype(np.float32)
+    sb = (r.random(N) * 1e-3 + 1e-4).astype(np.float32)
+    bias = torch.from_numpy((r.standard_normal(N) * 0.1).astype(np.float32)).to(torch.bfloat16)
+    y = ops.gemm_i8(cu(a), cu(b), cu(sa), L.QI8_S_ROW, cu(sb), L.QI8_S_ROW, bias.to(dev()), dtype)
+    ref = O.linear_w8a8_epilogue(O.int_mm(a, b), sa, sb, bias.float().numpy())
+    if dtype == torch.bfloat16:
+        assert np.array_equal(bf16_bits(y), O.f32_to_bf16(ref))
+    else:
+        assert np.array_equal(np_(y), ref)
 
 
 def test_gemm_gelu_epilogue():
