@@ -546,6 +546,59 @@ __device__ __forceinline__ void plain_epilogue32(const uint32_t (&acc)[32], floa
   }
 }
 
+// The transposed form of plain_epilogue32 (weights on the TMEM lanes): the
+// thread is output feature n with weight scale frow and bias brow, its 32
+// values are tokens m0 .. m0 + 31 with the staged token scales col[j]:
+//   y[j] = float(acc[j]) * (frow * col[j]) + brow, then the optional GELU;
+// frow * col[j] is the same rounded product as the untransposed x_s * w_s.
+__device__ __forceinline__ void swap_epilogue32(const uint32_t (&acc)[32], float frow, const float* col, float brow,
+                                                bool has_bias, int act, int out_dtype, float (&y)[32]) {
+  const float4* c4 = reinterpret_cast<const float4*>(col);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 s = c4[q];
+    const float sv[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) y[4 * q + u] = __fmul_rn(__int2float_rn((int)acc[4 * q + u]), __fmul_rn(frow, sv[u]));
+  }
+  if (has_bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], brow);
+  }
+  if (act == QI8_ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = act_gelu(y[j], out_dtype);
+  }
+}
+
+__device__ __forceinline__ uint16_t bits16(float v, int out_dtype) {
+  return out_dtype == QI8_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+}
+
+// Stores the warp's transposed 32 x 32 tile (lane = feature nb + lane,
+// y[j] = token m0 + j) as rows of the 16-bit output: each lane writes its
+// column into a per-warp shared tile of 32 rows x 40 halfwords (80-byte rows:
+// the column writes and the 16-byte row reads are bank-conflict free), then
+// lane l stores token m0 + l's 32 features as four 16-byte stores; features
+// >= N (N is a multiple of 16) and tokens >= M are skipped.
+constexpr int SWAP_TILE_LD = 40;
+__device__ __forceinline__ void store_tile32_swap(const GemmArgs& p, uint16_t* tile, int nb, int m0,
+                                                  const float (&y)[32], int lane) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) tile[j * SWAP_TILE_LD + lane] = bits16(y[j], p.out_dtype);
+  __syncwarp();
+  const int m = m0 + lane;
+  if (m < p.M) {
+    const uint4* src = reinterpret_cast<const uint4*>(tile + lane * SWAP_TILE_LD);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (int64_t)m * p.ld_out + nb);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (nb + 8 * q + 8 <= p.N) dst[q] = src[q];
+  }
+  // the tile is rewritten by this warp's next chunk
+  __syncwarp();
+}
+
 // Tile epilogue of the block-scaled kernels: final scales, optional GELU and
 // the stores, from the WC accumulator registers of one thread.
 // SWAP: thread = output feature rr, the 128 values are tokens cc0..cc0+127;
@@ -1114,7 +1167,12 @@ __host__ __device__ constexpr uint32_t idesc_pair(int n) {
 }
 constexpr uint32_t IDESC_P256 = idesc_pair(256);
 constexpr int P_NUM_BARS = 2 * P_STAGES + 2 * P_BUFS + 1;  // full, empty, tfull, tempty, drain
-constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * 2 * 16 * 32 * 2;
+// column scales, bias, K-block scales; then the per-warp transpose tiles
+// (the block-scaled finalize uses 2 x 16 x 32 bf16 of each warp's share,
+// the transposed plain epilogue 32 x SWAP_TILE_LD halfwords)
+constexpr int P_SWAP_TILE = 32 * SWAP_TILE_LD;  // halfwords per warp
+static_assert(P_SWAP_TILE >= 2 * 16 * 32, "transpose tile");
+constexpr int P_SCRATCH = 3 * NUM_EPI_WARPS * 128 * 4 + NUM_EPI_WARPS * P_SWAP_TILE * 2;
 constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE_BYTES + P_SCRATCH + P_NUM_BARS * 8 + 16;
 static_assert(P_SMEM <= 232448, "shared memory");
 
@@ -1178,7 +1236,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   float* scol = reinterpret_cast<float*>(sb + P_STAGES * P_STAGE_BYTES);  // [8 warps][128] column scales
   float* sbias = scol + NUM_EPI_WARPS * 128;                              // [8 warps][128] bias
   float* skb = sbias + NUM_EPI_WARPS * 128;                               // [8 warps][128] per-kb scales
-  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][2][16][32]
+  __nv_bfloat16* sxp = reinterpret_cast<__nv_bfloat16*>(skb + NUM_EPI_WARPS * 128);  // [8 warps][P_SWAP_TILE] transpose tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sb + P_STAGES * P_STAGE_BYTES + P_SCRATCH);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P_NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -1501,24 +1559,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        // rounds of 64 columns: two for 256-wide tiles, one for 128-wide
-        const int nrnd = half >> 6;
-#pragma unroll 2
-        for (int rnd = 0; rnd < nrnd; ++rnd) {
+        // chunks of 32 columns, loaded two at a time: half / 32 of them
+        // (4 for 256-wide tiles, 3 for 192, 2 for 128, 1 for 64)
+        const int nch = half >> 5;
+#pragma unroll 1
+        for (int ch = 0; ch < nch; ch += 2) {
+          const bool two = ch + 1 < nch;  // warp-uniform
           uint32_t r[2][32];
-          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * half + rnd * 64);
+          const uint32_t ta = tmem_base + lane_base + (uint32_t)(buf * PBN + cg * half + ch * 32);
           tmem_ld32(ta, r[0]);
-          tmem_ld32(ta + 32, r[1]);
+          if (two) tmem_ld32(ta + 32, r[1]);
           tmem_wait_ld();
-          if (rnd == nrnd - 1) {
+          if (ch + 2 >= nch) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_cluster(tempty0 + (uint32_t)(buf * 8));
           }
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const int cc = rnd * 64 + c * 32;
+            if (c == 1 && !two) break;
+            const int cc = ch * 32 + c * 32;
             const int n0 = cc0 + cc;
+            if constexpr (SWAP) {
+              // weights on the lanes: rr is feature n, the 32 columns are tokens n0 ..
+              if (n0 >= p.M || rr - lane >= p.N) continue;  // warp-uniform
+              float y[32];
+              swap_epilogue32(r[c], frow, my_col + cc, brow, p.bias != nullptr, p.act, p.out_dtype, y);
+              store_tile32_swap(p, reinterpret_cast<uint16_t*>(sxp) + warp * P_SWAP_TILE, rr - lane, n0, y, lane);
+              continue;
+            }
             if constexpr (MULTI) {
               // peer destinations: the warp's 32 x 32 tile goes through shared
               // memory so that each store writes 64 contiguous bytes of a row
@@ -1710,6 +1779,29 @@ __global__ void splitk_finalize_kernel(const int32_t* __restrict__ ws, int S, in
   }
 }
 
+// Tile width in tokens (64 or 128) of an unsplit plain GEMM of at most 128
+// tokens run with the weights on the TMEM lanes, or 0 when that does not pad
+// the work (padded lanes x padded columns) by at least 10 % less than the
+// single-CTA kernel's 128-row tiles.  Larger token counts stay on the lanes:
+// 576 tokens as 3 x 192-token tiles measured 8 % slower than 3 x 256-row
+// tiles at K = 3072, where the per-tile epilogue (here with the transposed
+// store) and not the MMAs sets the tile time.
+int plain_swap_width(int64_t M, int64_t N) {
+  if (M <= 0 || M > BM) return 0;
+  int best = 0;
+  int64_t best_pad = 0;
+  for (int w = 256; w >= 64; w -= 64) {
+    const int64_t pad = (M + w - 1) / w * w;
+    if (best == 0 || pad < best_pad) {
+      best = w;
+      best_pad = pad;
+    }
+  }
+  const int64_t n_pad = (N + 255) / 256 * 256;
+  const int64_t m_lanes = M <= BM ? BM : (M + 255) / 256 * 256;
+  return n_pad * best_pad * 10 <= m_lanes * n_pad * 9 ? best : 0;
+}
+
 // K splits of a plain-scale GEMM on the pair kernel: only when its tiles
 // fill at most half of the co-resident CTA pairs, K has >= 64 blocks
 // (K >= 8192) and every split keeps >= 8 blocks.  Measured as device time
@@ -1783,24 +1875,29 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
   }
   if (M == 0) return QI8_OK;
 
-  // weights on TMEM lanes when their scale varies per (row, K block) and the activations' does not
-  const bool swap = promote && b_kind == QI8_S_ROW_KBLOCK && a_kind != QI8_S_ROW_KBLOCK;
-  const int8_t* Rop = swap ? B : A;
-  const int8_t* Cop = swap ? A : B;
-  const int64_t Rrows = swap ? N : M, Crows = swap ? M : N;
   int dev = 0;
   QI8_CUDA(cudaGetDevice(&dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // a plain GEMM whose output tiles fill few CTA pairs splits K when the
-  // caller gives a workspace, also with at most 128 rows (the pair tile's
-  // rows beyond M are zero-filled by TMA and never stored)
-  bool split_small = false;
-  if (Rrows <= BM && !promote && n_outs == 1 && workspace && out_dtype != QI8_I8) {
-    int kb_split = 0;
-    const int S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
-    split_small = S > 1 && workspace_bytes >= (int64_t)S * M * N * 4;
+  // caller gives a workspace and K is long, also with at most 128 rows (the
+  // pair tile's rows beyond M are zero-filled by TMA and never stored)
+  int S = 1, kb_split = (int)((K + BK - 1) / BK);
+  if (!promote && n_outs == 1 && workspace && aligned16(workspace)) {
+    S = choose_splits(M, N, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
+    if (S > 1 && workspace_bytes < (int64_t)S * M * N * 4) S = 1;
   }
-  if (Rrows > BM || split_small) {
+  // weights on TMEM lanes when their scale varies per (row, K block) and the
+  // activations' does not; for an unsplit plain GEMM with 16-bit output and
+  // at most 128 tokens, when the tokens pad less as a tile width (64 tokens:
+  // one 64-wide tile instead of a 128-row lane tile)
+  const int swap_pbn = (!promote && n_outs == 1 && S == 1 && (out_dtype == QI8_BF16 || out_dtype == QI8_F16))
+                           ? plain_swap_width(M, N)
+                           : 0;
+  const bool swap = (promote && b_kind == QI8_S_ROW_KBLOCK && a_kind != QI8_S_ROW_KBLOCK) || swap_pbn > 0;
+  const int8_t* Rop = swap ? B : A;
+  const int8_t* Cop = swap ? A : B;
+  const int64_t Rrows = swap ? N : M, Crows = swap ? M : N;
+  if (Rrows > BM || S > 1 || swap_pbn > 0) {
     // CTA pairs: 256 rows on TMEM lanes x bnp columns per pair tile.  A
     // plain GEMM with few tiles splits K (caller workspace, long K), or
     // else, when even the 128-column tiles fill at most half of the pairs,
@@ -1808,13 +1905,8 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
     // narrow tiles cost more L2 traffic and epilogue per multiply-add: a
     // rule of tiles * 2 <= pairs measured slower on the linear stacks,
     // whose second stream's GEMM runs on the pairs a lone GEMM leaves idle.
-    int S = 1, kb_split = (int)((K + BK - 1) / BK);
-    if (!promote && n_outs == 1 && workspace && aligned16(workspace)) {
-      S = choose_splits(Rrows, Crows, K, pair_max_clusters<false, false, false, true>(dev), &kb_split);
-      if (S > 1 && workspace_bytes < (int64_t)S * M * N * 4) S = 1;
-    }
-    int bnp = pairk::PBN;
-    if (S == 1 && !promote && n_outs == 1) {
+    int bnp = swap_pbn > 0 ? swap_pbn : pairk::PBN;
+    if (S == 1 && !promote && n_outs == 1 && swap_pbn == 0) {
       const int64_t tiles = ((Rrows + 255) / 256) * ((Crows + pairk::PBN - 1) / pairk::PBN);
       const int maxc = pair_max_clusters<false, false, false, false>(dev);
       if (maxc > 0 && tiles * 4 <= maxc) bnp = pairk::PBN / 2;
@@ -1869,7 +1961,10 @@ int gemm_launch(const int8_t* A, const int8_t* B, int64_t M, int64_t N, int64_t 
       if (swap) return launch_pair<true, true, true>(mapA, mapB, p, e, dev, st);
       return launch_pair<true, false, true>(mapA, mapB, p, e, dev, st);
     }
-    if (!promote) return launch_pair<false, false, false>(mapA, mapB, p, e, dev, st);
+    if (!promote) {
+      if (swap) return launch_pair<false, true, false>(mapA, mapB, p, e, dev, st);
+      return launch_pair<false, false, false>(mapA, mapB, p, e, dev, st);
+    }
     if (swap) return launch_pair<true, true, false>(mapA, mapB, p, e, dev, st);
     return launch_pair<true, false, false>(mapA, mapB, p, e, dev, st);
   }

@@ -354,6 +354,46 @@ def test_gemm_few_tiles_epilogue_bitexact(M, N, K, dtype):
         assert np.array_equal(np_(y), ref)
 
 
+@pytest.mark.parametrize("M,N,K,dtype,bias,act", [
+    (64, 3072, 1024, torch.bfloat16, True, L.QI8_ACT_NONE),     # one 64-token tile
+    (64, 3072, 512, torch.bfloat16, True, L.QI8_ACT_GELU),
+    (40, 1024, 256, torch.bfloat16, False, L.QI8_ACT_NONE),
+    (1, 512, 2048, torch.bfloat16, True, L.QI8_ACT_NONE),
+    (33, 1040, 256, torch.float16, False, L.QI8_ACT_NONE),      # ragged features: the last lane tile holds 16
+    (576, 3072, 1024, torch.bfloat16, True, L.QI8_ACT_NONE),    # more than 128 tokens stay on the lanes
+])
+def test_gemm_weights_on_lanes_bitexact(M, N, K, dtype, bias, act):
+    """Unsplit plain GEMMs of at most 64 tokens run with the weights on the
+    TMEM lanes and the tokens as a 64-wide tile, stored through a per-warp
+    transpose.  Every output equals the
+    tokens-on-lanes kernel's (the same tokens zero-padded to a multiple of
+    256 rows, which keeps them on the lanes) bit for bit, and without GELU
+    the oracle's epilogue in bf16/f16."""
+    r = rng(M + 5 * N + K)
+    a = r.integers(-128, 128, (M, K), dtype=np.int8)
+    b = r.integers(-127, 128, (N, K), dtype=np.int8)
+    sa = (r.random((M, 1)) * 0.01 + 1e-3).astype(np.float32)
+    sb = (r.random(N) * 1e-3 + 1e-4).astype(np.float32)
+    bt = torch.from_numpy((r.standard_normal(N) * 0.1).astype(np.float32)).to(torch.bfloat16) if bias else None
+    y = ops.gemm_i8(cu(a), cu(b), cu(sa), L.QI8_S_ROW, cu(sb), L.QI8_S_ROW,
+                    None if bt is None else bt.to(dev()), dtype, act=act)
+    Mp = (M + 255) // 256 * 256
+    ap = np.zeros((Mp, K), np.int8)
+    ap[:M] = a
+    sap = np.full((Mp, 1), 1e-3, np.float32)
+    sap[:M] = sa
+    yl = ops.gemm_i8(cu(ap), cu(b), cu(sap), L.QI8_S_ROW, cu(sb), L.QI8_S_ROW,
+                     None if bt is None else bt.to(dev()), dtype, act=act)
+    assert torch.equal(y, yl[:M])
+    if act == L.QI8_ACT_GELU:
+        return
+    ref = O.linear_w8a8_epilogue(O.int_mm(a, b), sa, sb, None if bt is None else bt.float().numpy())
+    if dtype == torch.bfloat16:
+        assert np.array_equal(bf16_bits(y), O.f32_to_bf16(ref))
+    else:
+        assert np.array_equal(np_(y).view(np.uint16), ref.astype(np.float16).view(np.uint16))
+
+
 def test_gemm_gelu_epilogue():
     r = rng(3)
     M, N, K = 200, 512, 512
