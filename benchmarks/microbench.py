@@ -94,7 +94,8 @@ def gemm_cases(run, dev):
         res[f"k2_block_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
         us = run(lambda: ops.gemm_i8(a, b, sa, L.QI8_S_ROW, sb, L.QI8_S_ROW, None, torch.bfloat16, out=out))
         res[f"k2_row_{M}x{N}x{K}"] = [us, 2 * M * N * K / us / 1e6]
-    # the rotated single linear's GEMM (512 tokens, tensorwise weight scale, fp32 out): split-K vs one pass
+    # the rotated single linear's GEMM (512 tokens, tensorwise weight scale, fp32 out): the workspace entry
+    # (splits K only from K = 8192, so this shape runs one pass) and the plain entry
     M, N, K = 512, 4096, 4096
     a = torch.randint(-128, 128, (M, K), dtype=torch.int8, device=dev)
     b = torch.randint(-128, 128, (N, K), dtype=torch.int8, device=dev)
