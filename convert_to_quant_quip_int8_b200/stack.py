@@ -14,11 +14,12 @@ whole forward can be captured once and replayed as a CUDA graph.
   8 x 512 tokens; axis-wise weight scales ``[N]``
   (``AxisWiseINT8Layout``, comfy/quant_ops.py:330-339).
 
-Independent linears overlap: a double block's txt linears (and T5's k next
-to q and v, wi_1 next to wi_0) run on a second stream of the captured graph,
-forked at the start of their group and joined at its end, with their own
-quantization, workspace and output buffers.  Small per-rank GEMMs of a token
-split fill few CTA pairs, so the other lane's GEMM runs on the idle SMs.
+Independent linears overlap: a double block's txt linears (and T5's q, k
+and v, wi_0 and wi_1) run on their own streams ("lanes") of the captured
+graph, forked at the start of their group and joined at its end, each lane
+with its own quantization, workspace and output buffers.  Small per-rank
+GEMMs of a token split fill few CTA pairs, so another lane's GEMM runs on
+the idle SMs.
 
 Each linear is the reference's W8A8 forward (comfy/quant_ops.py:461-475):
 per-token int8 quantization of the bf16 input (K1), then the int8 GEMM with
@@ -63,7 +64,7 @@ class LinearSpec:
     n: int
     src: str = "x"      # "x": synthetic activation [tokens, k]; otherwise the linear whose output feeds this one
     gelu: bool = False  # GELU of the input, fused into the per-token quantization
-    lane: int = 0       # 1: runs on the second stream, concurrently with lane 0 of its group
+    lane: int = 0       # > 0: runs on that lane's stream, concurrently with the other lanes of its group
     group: str = ""     # consecutive specs of one non-empty group fork at its start and join at its end
 
 
@@ -82,7 +83,7 @@ def flux_specs() -> List[LinearSpec]:
 
 def t5_specs() -> List[LinearSpec]:
     # q, k, v read the same input; so do wi_0 and wi_1
-    lane = {"k": 1, "wi_1": 1}
+    lane = {"k": 1, "v": 2, "wi_1": 1}
     group = {"q": "qkv", "k": "qkv", "v": "qkv", "wi_0": "wi", "wi_1": "wi"}
     specs = []
     for name, t, k, n in t5_linears():
@@ -105,7 +106,7 @@ STACKS = {
 def fork_groups(specs: List[LinearSpec]) -> List[Tuple[List[int], bool]]:
     """Consecutive specs of one non-empty group form a group; every other
     spec is a group of its own.  Returns (spec indices, forks) per group in
-    order, where ``forks`` says whether the group has lane-1 linears."""
+    order, where ``forks`` says whether the group has linears on lanes > 0."""
     groups: List[List[int]] = []
     for i, sp in enumerate(specs):
         if groups and sp.group and specs[i - 1].group == sp.group:
@@ -137,11 +138,14 @@ class LinearStack:
                           for sp in self.specs]
         self.rank, self.world, self.group = rank, world, group
         self.sharded = shard == "columns" and world > 1
-        # the second stream only where lanes exist and no collective orders the linears
+        # lane streams only where lanes exist and no collective orders the linears
         self.overlap = overlap and not self.sharded and any(sp.lane for sp in self.specs)
-        self.side = torch.cuda.Stream(device) if self.overlap else None
+        lanes = sorted({sp.lane for sp in self.specs if sp.lane}) if self.overlap else []
+        self.sides = {ln: torch.cuda.Stream(device) for ln in lanes}
         self.groups = fork_groups(self.specs) if self.overlap else [([i], False) for i in range(len(self.specs))]
-        self.fork_events = [(torch.cuda.Event(), torch.cuda.Event()) for ix, f in self.groups if f]
+        # per forked group: the fork event, and a join event per lane
+        self.fork_events = [(torch.cuda.Event(), {ln: torch.cuda.Event() for ln in self.sides})
+                            for ix, f in self.groups if f]
         self.chunks = chunks
         self.gather = gather  # column mode: "peer" (fused into the GEMM epilogue) or "nccl"
         self.peer = None
@@ -319,28 +323,32 @@ class LinearStack:
         """One forward on the current stream.  With ``events`` (a start/end
         event pair per linear around its GEMM launches) every linear runs on
         the current stream in spec order, so each GEMM is timed alone;
-        otherwise each group with lane-1 linears forks them onto the second
-        stream and joins it at the group's end (graph-capturable)."""
+        otherwise each group with linears on lanes > 0 forks them onto their
+        lanes' streams and joins them at the group's end (graph-capturable)."""
         sp = L.stream_ptr(self.device)
         if events is not None or not self.overlap:
             for i in range(len(self.specs)):
                 self.run_linear(i, sp, None if events is None else events[i])
             return
         main = torch.cuda.current_stream(self.device)
-        side = ctypes.c_void_p(self.side.cuda_stream)
+        ptrs = {ln: ctypes.c_void_p(st.cuda_stream) for ln, st in self.sides.items()}
         forks = iter(self.fork_events)
         for ix, forked in self.groups:
             if not forked:
                 for i in ix:
                     self.run_linear(i, sp)
                 continue
-            fork, join = next(forks)
+            fork, joins = next(forks)
+            used = sorted({self.specs[i].lane for i in ix if self.specs[i].lane})
             fork.record(main)
-            self.side.wait_event(fork)
+            for ln in used:
+                self.sides[ln].wait_event(fork)
             for i in ix:
-                self.run_linear(i, side if self.specs[i].lane else sp)
-            join.record(self.side)
-            main.wait_event(join)
+                ln = self.specs[i].lane
+                self.run_linear(i, ptrs[ln] if ln else sp)
+            for ln in used:
+                joins[ln].record(self.sides[ln])
+                main.wait_event(joins[ln])
 
     def launches_per_forward(self) -> int:
         """Kernels of this library launched by one forward (K1 + GEMMs + layouts)."""

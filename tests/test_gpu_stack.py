@@ -121,15 +121,16 @@ def test_stack_token_split_rank_specs_and_rows():
 
 
 def test_stack_lanes_overlap_equals_sequential():
-    """Two lanes of a group (the second on its own stream, forked at the
-    group's start and joined at its end): the overlapped forward, eager and
-    replayed as a graph, writes the same bits as the linears run one at a
-    time; a lane-0 linear after the join reads the lane-1 output."""
+    """Three lanes of a group (lanes 1 and 2 on their own streams, forked
+    at the group's start and joined at its end): the overlapped forward,
+    eager and replayed as a graph, writes the same bits as the linears run
+    one at a time; a lane-0 linear after the join reads the lane-1 output."""
     dev = torch.device("cuda", 0)
     specs = [LinearSpec("g.img.mlp0", 200, 256, 512, lane=0, group="g"),
              LinearSpec("g.img.mlp2", 200, 512, 256, "g.img.mlp0", True, 0, "g"),
              LinearSpec("g.txt.mlp0", 64, 256, 512, lane=1, group="g"),
              LinearSpec("g.txt.mlp2", 64, 512, 256, "g.txt.mlp0", True, 1, "g"),
+             LinearSpec("g.aux.proj", 96, 256, 192, lane=2, group="g"),
              LinearSpec("h.proj", 64, 256, 384, "g.txt.mlp2"),
              LinearSpec("h.out", 64, 384, 128, "h.proj"),
              LinearSpec("k.other", 200, 256, 128, "g.img.mlp2")]
@@ -140,13 +141,13 @@ def test_stack_lanes_overlap_equals_sequential():
         seq.run_linear(i, sp)
         ref[s.name] = seq.out_of[s.name].clone()
     ovl = LinearStack("flux", dev, specs=specs)
-    assert ovl.overlap and ovl.side is not None
+    assert ovl.overlap and sorted(ovl.sides) == [1, 2]
     assert [f for _, f in ovl.groups] == [True, False, False, False]
     for key, x in ovl.inputs.items():
         assert torch.equal(x, seq.inputs[key])
     ovl.forward()
     torch.cuda.synchronize()
-    kept_or_last = ["g.img.mlp0", "g.img.mlp2", "g.txt.mlp0", "g.txt.mlp2", "h.proj", "k.other"]
+    kept_or_last = ["g.img.mlp0", "g.img.mlp2", "g.txt.mlp0", "g.txt.mlp2", "g.aux.proj", "h.proj", "k.other"]
     for name in kept_or_last:
         assert torch.equal(ovl.out_of[name], ref[name]), name
     g = torch.cuda.CUDAGraph()

@@ -124,9 +124,10 @@ def test_conversion_driver_selects_2d_weights_and_names_shards():
 
 
 def test_stack_fork_groups():
-    """The Flux stack forks each double block's txt linears onto the second
-    lane (19 groups of 8, the single blocks alone); T5 forks q/k/v and
-    wi_0/wi_1 of every layer; a token split keeps lanes and groups."""
+    """The Flux stack forks each double block's txt linears onto lane 1
+    (19 groups of 8, the single blocks alone); T5 runs q, k, v on lanes
+    0, 1, 2 and wi_0, wi_1 on lanes 0, 1 of every layer; a token split
+    keeps lanes and groups."""
     from convert_to_quant_quip_int8_b200.stack import LinearSpec, flux_specs, fork_groups, t5_specs
     fx = flux_specs()
     g = fork_groups(fx)
@@ -145,7 +146,7 @@ def test_stack_fork_groups():
     g5 = fork_groups(t5)
     assert sum(1 for _, f in g5 if f) == 48 and len(g5) == 24 * 4
     assert [t5[i].name.split(".")[1] for i in g5[0][0]] == ["q", "k", "v"]
-    assert [t5[i].lane for i in g5[0][0]] == [0, 1, 0]
+    assert [t5[i].lane for i in g5[0][0]] == [0, 1, 2]
     # groups only join consecutive specs
     specs = [LinearSpec("a", 8, 16, 16, group="g"), LinearSpec("b", 8, 16, 16, lane=1, group="g"),
              LinearSpec("c", 8, 16, 16), LinearSpec("d", 8, 16, 16, lane=1, group="g")]
