@@ -611,6 +611,7 @@ def main_stack(args):
                                            "orig_dtype": torch.bfloat16}) for q, sc, _ in st.weights]
         apply = lambda i, x: F.linear(x, qts[i], st.weights[i][2])
     host_in = st.host_inputs()
+    consumed = {t.src for t in st.specs if t.src != "x"}  # outputs a later linear reads
     last = st.specs[-1]
     y_host = torch.empty(last.tokens, last.n, dtype=torch.bfloat16).pin_memory()
 
@@ -643,7 +644,7 @@ def main_stack(args):
             else:
                 x = F.gelu(kept.pop(s.src))
             y = apply(i, x)
-            if any(t.src == s.name for t in st.specs):
+            if s.name in consumed:
                 kept[s.name] = y
         y_host.copy_(y, non_blocking=True)
 
